@@ -1,0 +1,399 @@
+"""Benchmark of the optimizer-step path on B200 (and of the reference's CPU path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one full TritonMuonSRWithAuxAdam(batch_ns=True) step on
+Llama-3-8B-shaped synthetic tensors -- 224 hidden matrices in the Muon group (lr 0.02,
+momentum 0.95, Nesterov, ns_steps 5, wd 0.01), embedding, head and 65 RMSNorm vectors in
+the AdamW group -- bf16 params ~N(0, 0.02), grads ~N(0, 1e-3), seeded. Every tensor is far
+larger than the 126 MB L2, so timed steps stream from HBM without an explicit flush.
+The same run also times the 8-bit blockwise AdamW step on the same tensors.
+
+``value`` is the device time of one full step (max over ranks, CUDA events), ``e2e`` the
+same step through the public API with the step's gradients copied in from pinned host
+memory and the updated weights copied back out. ``--impl reference`` times the
+reference's pure-PyTorch MuonSR / AdamW-SR step (restated in ``oracle/``) on the host
+cores on a bounded sample and scales it to a full step.
+"""
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "Llama-3-8B hybrid optimizer step ms; NS TFLOP/s; 8-bit AdamW HBM GB/s"
+N_LAYERS, D, KV, FF, VOCAB = 32, 4096, 1024, 14336, 128256
+
+
+def llama_shapes():
+    muon = []
+    for _ in range(N_LAYERS):
+        muon += [(D, D), (KV, D), (KV, D), (D, D), (FF, D), (FF, D), (D, FF)]
+    adam = [(VOCAB, D), (VOCAB, D)] + [(D,)] * (2 * N_LAYERS + 1)
+    return muon, adam
+
+
+def ns_flops(shape, steps=5):
+    m, n = min(shape), max(shape)
+    return steps * (4 * m * m * n + 2 * m ** 3)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+class Timers:
+    """CUDA-event timers around the kernel wrappers (current stream), summed per name."""
+
+    def __init__(self):
+        self.events = {}
+        self.enabled = False
+
+    def wrap(self, mod, name):
+        fn = getattr(mod, name)
+        timers = self
+
+        def timed(*a, **k):
+            if not timers.enabled:
+                return fn(*a, **k)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*a, **k)
+            e.record()
+            timers.events.setdefault(name, []).append((s, e))
+            return out
+
+        setattr(mod, name, timed)
+
+    def totals_ms(self):
+        return {k: sum(s.elapsed_time(e) for s, e in v) for k, v in self.events.items()}
+
+    def counts(self):
+        return {k: len(v) for k, v in self.events.items()}
+
+
+def build_tensors(device, seed=0):
+    muon_shapes, adam_shapes = llama_shapes()
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def mk(shape, std):
+        t = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        t.normal_(0.0, std, generator=g)
+        return torch.nn.Parameter(t)
+
+    muon = [mk(s, 0.02) for s in muon_shapes]
+    adam = [mk(s, 0.02) for s in adam_shapes]
+    for p in muon + adam:
+        p.grad = torch.empty_like(p).normal_(0.0, 1e-3, generator=g)
+    return muon, adam
+
+
+def time_steps(step_fn, steps, warmup, world):
+    for _ in range(warmup):
+        step_fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step_fn()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    return ms
+
+
+def run_ours(args, rank, world, local_rank):
+    from muon_sr_b200 import Sharder, TritonAdamW8bit, TritonMuonSRWithAuxAdam, _lib
+    from muon_sr_b200 import kernels as K
+    from muon_sr_b200 import muon as M
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    lib = _lib.load()
+    hbm_gbs, tf_burst, tf_sus, peak_kind = peaks()
+    muon, adam = build_tensors(device)
+    shard = Sharder() if world > 1 else None
+    opt = TritonMuonSRWithAuxAdam([
+        dict(params=muon, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+        dict(params=adam, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
+    ], batch_ns=True, shard=shard)
+
+    timers = Timers()
+    for name in ("newton_schulz", "muon_prepare", "muon_apply", "adamw_sr"):
+        timers.wrap(K, name)
+    # the optimizer module imported the wrappers by module reference (K.<name>), so the
+    # wrapped functions are the ones it calls
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    l0 = lib.msr_launch_count()
+    timers.enabled = True
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    timers.events.clear()
+    l0 = lib.msr_launch_count()
+    ms = time_steps(opt.step, args.steps, 0, world)
+    launches = lib.msr_launch_count() - l0
+    clocks = sampler.stop()
+    tot = timers.totals_ms()
+    timers.enabled = False
+    assert K.device_error() == 0, "device wait timed out in a kernel"
+
+    # Newton-Schulz roofline: algorithmic FLOPs of the matrices this rank owned
+    owned_flops = 0
+    if shard is None:
+        owned_flops = sum(ns_flops(tuple(p.shape)) for p in muon)
+    else:
+        owned_flops = sum(ns_flops(tuple(p.shape)) for p in muon if shard._owner[id(p)] == shard.rank)
+    ns_ms_step = tot.get("newton_schulz", 0.0) / args.steps
+    ns_tflops = owned_flops / (ns_ms_step * 1e-3) / 1e12 if ns_ms_step > 0 else None
+    total_flops = sum(ns_flops(tuple(p.shape)) for p in muon)
+
+    # elementwise bytes (per step, whole job)
+    n_muon = sum(p.numel() for p in muon)
+    n_adam = sum(p.numel() for p in adam)
+    breakdown = {k: v / args.steps for k, v in tot.items()}
+
+    # ---- 8-bit blockwise AdamW on the same tensors ----
+    params = muon + adam
+    opt8 = TritonAdamW8bit([dict(params=params, optim_bits=8)], lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
+                           weight_decay=0.01, block_size=256, shard=shard)
+    a8_timers = Timers()
+    a8_timers.wrap(K, "adamw8bit")
+    a8_timers.enabled = True
+    for _ in range(args.warmup):
+        opt8.step()
+    torch.cuda.synchronize()
+    a8_timers.events.clear()
+    a8_step_ms = time_steps(opt8.step, args.steps, 0, world)
+    a8_kernel_ms = a8_timers.totals_ms().get("adamw8bit", 0.0) / args.steps
+    a8_timers.enabled = False
+    n_all = n_muon + n_adam
+    a8_bytes = n_all * 10 + 2 * 8 * math.ceil(n_all / 256)
+    if shard is not None:
+        owned = sum(p.numel() for p in params if shard._owner[id(p)] == shard.rank)
+        a8_bytes_rank = owned * 10 + 16 * owned / 256
+    else:
+        a8_bytes_rank = a8_bytes
+    a8_gbs = a8_bytes_rank / (a8_kernel_ms * 1e-3) / 1e9 if a8_kernel_ms > 0 else None
+    del opt8
+    for p in params:
+        pass
+    torch.cuda.empty_cache()
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        pin_g = [torch.empty(p.shape, dtype=torch.bfloat16, pin_memory=True) for p in params]
+        for h, p in zip(pin_g, params):
+            h.copy_(p.grad)
+        owned_ps = [p for p in params if shard is None or shard._owner[id(p)] == shard.rank]
+        pin_p = [torch.empty(p.shape, dtype=torch.bfloat16, pin_memory=True) for p in owned_ps]
+
+        def e2e_step():
+            for h, p in zip(pin_g, params):
+                p.grad.copy_(h, non_blocking=True)
+            opt.step()
+            for h, p in zip(pin_p, owned_ps):
+                h.copy_(p.detach(), non_blocking=True)
+
+        e2e_ms = time_steps(e2e_step, max(2, args.steps // 2), 1, world)
+        h2d = sum(p.numel() * 2 for p in params) * world
+        d2h = sum(p.numel() * 2 for p in params)
+        e2e = {"value": e2e_ms, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        del pin_g, pin_p
+
+    result = None
+    if rank == 0:
+        peak_ns = tf_sus
+        result = {
+            "metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) params, N(0,1e-3) grads)",
+            "config": {"workload": "configs[3]: TritonMuonSRWithAuxAdam(batch_ns=True) step, Llama-3-8B shapes",
+                       "muon_matrices": len(muon), "adamw_tensors": len(adam), "elements": n_all,
+                       "parallelism": f"param-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs > L2 (126 MB), no flush"},
+            "ns_tflops": ns_tflops, "ns_tflop_per_step": total_flops / 1e12,
+            "adamw8bit_hbm_gbs": a8_gbs, "adamw8bit_step_ms": a8_step_ms, "adamw8bit_kernel_ms": a8_kernel_ms,
+            "breakdown_ms_per_step": breakdown,
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (Newton-Schulz chain)",
+                         "achieved": ns_tflops, "peak": peak_ns, "unit": "TFLOP/s",
+                         "frac": (ns_tflops / peak_ns) if ns_tflops else None,
+                         "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None},
+            "roofline_8bit": {"bound": "hbm", "kernel": "adamw8bit_kernel", "achieved": a8_gbs, "peak": hbm_gbs,
+                              "unit": "GB/s", "frac": (a8_gbs / hbm_gbs) if a8_gbs else None,
+                              "algorithmic_bytes": a8_bytes, "traffic": None},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "e2e": e2e,
+        }
+    return result
+
+
+# ---------------------------------------------------------------------------------------
+# CPU (reference) arm -- the reference's pure-PyTorch MuonSR / AdamW-SR restated in oracle/
+# ---------------------------------------------------------------------------------------
+def cpu_sample_step(threads):
+    """One bounded sample of the full Llama step on the host cores: one q_proj-shaped
+    (4096 x 4096) MuonSR parameter step and an AdamW-SR step on a 2^22-element slice.
+    Returns (seconds of the sample, extrapolation factor to a full step)."""
+    from oracle.muon_cpu import adamw_sr_step, muon_sr_step
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    shape = (D, D)
+    p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+    gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
+    b = torch.zeros_like(p)
+    n_slice = 1 << 22
+    pa = (torch.randn(n_slice, generator=g) * 0.02).bfloat16()
+    ga = (torch.randn(n_slice, generator=g) * 1e-3).bfloat16()
+    ea, eb = torch.zeros_like(pa), torch.zeros_like(pa)
+    t0 = time.perf_counter()
+    muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
+    t1 = time.perf_counter()
+    adamw_sr_step([pa], [ga], [ea], [eb], 1, weight_decay=0.01)
+    t2 = time.perf_counter()
+    muon_shapes, adam_shapes = llama_shapes()
+    f_total = sum(ns_flops(s) for s in muon_shapes)
+    n_adam = sum(math.prod(s) for s in adam_shapes)
+    full = (t1 - t0) * f_total / ns_flops(shape) + (t2 - t1) * n_adam / n_slice
+    return full * 1e3, t2 - t0
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    sample = ("per step: one 4096x4096 MuonSR parameter step (oracle.muon_cpu, restating muon_sr/muon_sr.py) "
+              "scaled by Newton-Schulz FLOPs to all 224 matrices, plus a 4.2M-element AdamW-SR slice scaled "
+              "by elements to the 1.05G-element AdamW group")
+    for _ in range(args.warmup):
+        cpu_sample_step(threads)
+    vals = [cpu_sample_step(threads)[0] for _ in range(args.steps)]
+    v = statistics.median(vals)
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "ms", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "configs[3]: hybrid Muon+AdamW SR step, Llama-3-8B shapes (CPU, sampled)"},
+            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        out = run_reference(args, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        out = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                v, secs = cpu_sample_step(os.cpu_count() or 1)
+                out["cpu_baseline"] = {"value": v, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
+                                       "sample": f"one 4096x4096 MuonSR step + 4.2M-element AdamW-SR slice "
+                                                 f"({secs:.1f} s of CPU work), scaled to the full step"}
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,186 @@
+/*
+ * muon_sr_b200 -- C ABI of the B200 (sm_100a) optimizer-step engine.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream
+ * (cudaStream_t passed as an opaque handle), enqueues its kernels on that stream and
+ * returns an msr_status. Nothing here allocates device memory: callers own every buffer
+ * (parameters, gradients, optimizer states and the Newton-Schulz workspace, whose size
+ * msr_ns_workspace_bytes reports). No entry point synchronises the stream except
+ * msr_device_error.
+ *
+ * The reference (bab2min/muon_sr 0.1.2) is a Python package whose device work is a set of
+ * Triton kernels plus torch.matmul; each entry point below replaces one of those launch
+ * sites and cites it. Random seeds are the 64-bit Philox keys that the reference's Triton
+ * kernels derive from their Python seed arguments; the Python layer of this package
+ * computes them with the reference's formulas (muon_sr/triton_muon_sr.py:83-85).
+ */
+#ifndef MUON_SR_B200_H
+#define MUON_SR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* msr_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+enum msr_status {
+  MSR_OK = 0,
+  MSR_ERR_INVALID = 1,        /* bad argument: null pointer, negative size, bad shape */
+  MSR_ERR_CUDA = 2,           /* a CUDA runtime call or kernel launch failed */
+  MSR_ERR_UNSUPPORTED = 3,    /* valid request this build cannot run (e.g. not sm_100) */
+  MSR_ERR_WORKSPACE = 4,      /* workspace smaller than msr_ns_workspace_bytes() */
+  MSR_ERR_DEVICE_TIMEOUT = 5  /* a kernel gave up on a barrier wait (see msr_device_error) */
+};
+
+/* Version of this ABI (bumped on any signature change). */
+int msr_abi_version(void);
+/* Static description of a status code. */
+const char* msr_status_string(int status);
+/* Detail message of the last failing call on the calling host thread ("" if none). */
+const char* msr_last_error(void);
+/* Synchronises `stream`, returns the device-side error code recorded by any kernel of
+ * this library since the last clear (0 = none) and clears it when `clear` != 0. */
+int msr_device_error(msr_stream_t stream, int clear);
+/* Number of kernels this library has launched in this process (all threads, all devices). */
+uint64_t msr_launch_count(void);
+
+/* ---- Philox (test hook) ------------------------------------------------------------
+ * out[i] = word 0 of Philox4x32-10 with counter ((ctr_base + i) mod 2^32, 0, 0, 0) and key
+ * `key`: Triton's tl.randint(seed, offset) as muon_sr's kernels call it
+ * (muon_sr/triton_muon_sr.py:44, muon_sr/triton_adamw.py:52). */
+int msr_philox_fill(uint32_t* out, int64_t n, uint64_t ctr_base, uint64_t key, msr_stream_t stream);
+
+/* ---- SR gradient accumulation ------------------------------------------------------
+ * acc[i] <- SR_bf16(float(acc[i]) + float(grad[i])), counter i. With first != 0 the
+ * accumulator is treated as zero and only written: acc[i] <- SR_bf16(0 + grad[i]), which is
+ * grad[i] itself except that -0 becomes +0 (the reference zero-fills, then accumulates).
+ * Replaces the _grad_accum_kernel launch of TritonSRAccumulator._accum_hook
+ * (muon_sr/triton_adamw.py:206-229, launched at :259-265). */
+int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, int first, msr_stream_t stream);
+
+/* ---- Muon momentum / Nesterov prepare ----------------------------------------------
+ * Per entry, per element i < numel:
+ *   new_buf = buf + one_minus_beta * (g - buf)
+ *   upd     = nesterov ? g + beta * (new_buf - g) : new_buf
+ *   momentum[i] <- SR_bf16(new_buf) with counter (ctr_base + i) mod 2^32
+ *   update[i]   <- RNE_bf16(upd)
+ *   *norm_sq    += sum_i float(update[i])^2      (if norm_sq != NULL; caller zeroes it)
+ * grad and update may alias (the reference prepares in place on its stacked workspace).
+ * Replaces _muon_prepare_kernel launches (muon_sr/triton_muon_sr.py:18-50, launched at
+ * :94-97 per parameter and :156-159 per shape stack, where ctr_base = index * numel). */
+typedef struct msr_prepare_entry {
+  const void* grad;    /* bf16[numel] */
+  void* momentum;      /* bf16[numel], updated in place */
+  void* update;        /* bf16[numel], output */
+  float* norm_sq;      /* optional fp32 accumulator */
+  int64_t numel;
+  uint64_t ctr_base;
+  uint64_t key;
+} msr_prepare_entry;
+
+int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta,
+                     int nesterov, msr_stream_t stream);
+
+/* ---- Muon apply ----------------------------------------------------------------------
+ * Per entry: param[i] <- SR_bf16(float(param[i]) * decay - lr * (float(update[i]) * scale)),
+ * counter i, with decay = fp32(1 - lr * weight_decay) computed by the caller in double.
+ * Replaces _muon_apply_kernel launches (muon_sr/triton_muon_sr.py:53-80, :105-113). */
+typedef struct msr_apply_entry {
+  void* param;         /* bf16[numel], updated in place */
+  const void* update;  /* bf16[numel] (Newton-Schulz output) */
+  int64_t numel;
+  uint64_t key;
+  float scale;         /* sqrt(max(1, rows/cols)) of the parameter's shape */
+  float reserved;
+} msr_apply_entry;
+
+int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float decay, msr_stream_t stream);
+
+/* ---- AdamW with stochastic rounding ------------------------------------------------
+ * Per entry, per element:
+ *   m = beta1*m + one_minus_beta1*g;  v = beta2*v + one_minus_beta2*g*g
+ *   denom = sqrt(v)/bc2_sqrt + eps;  p = p*decay;  p = p - step_size*m/denom
+ *   m, v, p <- SR_bf16 with keys key_m, key_v, key_p (the reference's seed, seed+1, seed+2)
+ * step_size = fp32(lr / (1 - beta1^step)), bc2_sqrt = fp32(sqrt(1 - beta2^step)).
+ * Replaces _adamw_kernel launches (muon_sr/triton_adamw.py:9-114). */
+typedef struct msr_adamw_entry {
+  void* param;
+  const void* grad;
+  void* exp_avg;
+  void* exp_avg_sq;
+  int64_t numel;
+  uint64_t key_m, key_v, key_p;
+  float step_size;
+  float bc2_sqrt;
+} msr_adamw_entry;
+
+typedef struct msr_adamw_hparams {
+  float beta1, one_minus_beta1, beta2, one_minus_beta2, eps, decay;
+} msr_adamw_hparams;
+
+int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp,
+                 msr_stream_t stream);
+
+/* ---- 8-bit blockwise AdamW -----------------------------------------------------------
+ * One pass per tensor: dequantise (codebook x block absmax), Adam moments with the
+ * non-finite-gradient mask, p' = (p - coef*m/(sqrt(v) + sqrt_bc2_eps)) * decay with SR
+ * (key_p), then per block of block_size elements absmax and requantise with the 7-step
+ * codebook search (quantized != 0), or SR bf16 moments (keys key_m, key_v) otherwise.
+ * coef = fp32(fp32(lr)*sqrt(bc2)/bc1), sqrt_bc2_eps = fp32(sqrt(bc2))*fp32(eps).
+ * Replaces _adamw_8bit_kernel launches (muon_sr/triton_adamw_8bit.py:56-99, :198-204). */
+typedef struct msr_adamw8bit_entry {
+  void* param;
+  const void* grad;
+  void* state1;        /* uint8 codes (quantized) or bf16 moments */
+  void* state2;
+  float* absmax1;      /* fp32[ceil(numel/block_size)] (quantized only) */
+  float* absmax2;
+  int64_t numel;
+  uint64_t key_p, key_m, key_v;
+  float coef;
+  float sqrt_bc2_eps;
+  int32_t quantized;
+  int32_t reserved;
+} msr_adamw8bit_entry;
+
+typedef struct msr_adamw8bit_hparams {
+  float beta1, one_minus_beta1, beta2, one_minus_beta2, decay;
+  int32_t block_size;  /* power of two in [32, 4096] */
+} msr_adamw8bit_hparams;
+
+int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, const float* qmap1,
+                  const float* qmap2, const msr_adamw8bit_hparams* hp, msr_stream_t stream);
+
+/* ---- Newton-Schulz ---------------------------------------------------------------------
+ * out[b] = NS_steps(x[b]) for b < batch, x and out bf16 [batch, rows, cols] contiguous.
+ * Quintic iteration (a, b, c) = (3.4445, -4.7750, 2.0315) on the wide orientation
+ * (X^T when rows > cols), normalised by 1/(||x[b]||_F + 1e-7). Each step is three
+ * batched tcgen05 GEMMs with fused epilogues: A = X X^T, B = c*(A A) + b*A,
+ * X' = B X + a*X. norm_sq, if given, holds ||x[b]||_F^2 (e.g. from msr_muon_prepare);
+ * otherwise it is computed. out must not alias x.
+ * Replaces _newton_schulz (muon_sr/muon_sr.py:82-98) with out_dtype=None, as called at
+ * muon_sr/triton_muon_sr.py:119 and :166. */
+size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
+
+int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
+                           int steps, const float* norm_sq, void* workspace, size_t workspace_bytes,
+                           msr_stream_t stream);
+
+/* ---- batched bf16 GEMM with the Newton-Schulz epilogue (test hook) --------------------
+ * d[b] = alpha_b * (A[b] x B[b]^T) + beta_b * c[b] on the tensor cores, bf16 in/out,
+ * fp32 accumulate. A is [batch, M, K] (a_mn_major = 0) or [batch, K, M] (1); B is
+ * [batch, N, K] (b_mn_major = 0) or [batch, K, N] (1); c, d are [batch, M, N]; c may be
+ * NULL. alpha_b = alpha * s^alpha_pow, beta_b = beta * s^beta_pow with s = scale[b]
+ * (scale may be NULL). Rows of every operand must be a multiple of 16 bytes. */
+int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c,
+                  void* d, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha, float beta,
+                  const float* scale, int alpha_pow, int beta_pow, msr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUON_SR_B200_H */

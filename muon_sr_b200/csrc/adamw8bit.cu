@@ -1,0 +1,350 @@
+// 8-bit blockwise AdamW with BF16 stochastic rounding of the weights, one HBM pass.
+//
+// Follows muon_sr/triton_adamw_8bit.py:27-99 (its _quantize and _adamw_8bit_kernel):
+// dequantise both moments with the dynamic codebooks and the per-block absmax, run the
+// Adam update with the non-finite-gradient mask, write the SR'd weight, then take the
+// block absmax of the new moments and requantise them with the reference's 7-step pivot
+// walk (bitsandbytes quantize_2D rules). Tensors below the 8-bit threshold keep bf16
+// moments with SR instead.
+//
+// Design (B200): each thread owns 8 consecutive elements (16-byte weight/gradient loads,
+// 8-byte code loads); a quantisation block of BS elements is BS/8 consecutive threads, so
+// the block absmax is a warp-shuffle reduction (plus shared memory when a block spans
+// warps). Both codebooks live in shared memory. A persistent grid walks tiles of
+// 256 threads x 8 (or x16 for BS = 4096) elements across all tensors of the launch.
+#include "common.cuh"
+#include "host_common.h"
+
+#include <algorithm>
+
+namespace msr {
+namespace {
+
+constexpr int Q_THREADS = 256;
+constexpr int Q_MAXE = 64;
+constexpr int Q_BLOCKS_PER_SM = 4;
+
+struct Adam8Args {
+  msr_adamw8bit_entry e[Q_MAXE];
+  int64_t prefix[Q_MAXE + 1];
+  uint8_t vec[Q_MAXE];
+  int count;
+  msr_adamw8bit_hparams hp;
+  const float* qmap1;
+  const float* qmap2;
+};
+
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+
+// _quantize -- muon_sr/triton_adamw_8bit.py:27-53
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t quantize(float x, const float* __restrict__ Q) {
+  int pivot = 127, lower_pivot = 0, upper_pivot = 255;
+  float lower = SIGNED ? -1.f : 0.f, upper = 1.f;
+  float val = Q[127];
+#pragma unroll
+  for (int s = 0; s < 7; ++s) {
+    const int delta = 64 >> s;
+    const bool right = x > val;
+    lower_pivot = right ? pivot : lower_pivot;
+    upper_pivot = right ? upper_pivot : pivot;
+    lower = right ? val : lower;
+    upper = right ? upper : val;
+    pivot += right ? delta : -delta;
+    val = Q[pivot];
+  }
+  int r;
+  if (x > val)
+    r = (x > fmul(fadd(upper, val), 0.5f)) ? upper_pivot : pivot;
+  else
+    r = (x < fmul(fadd(lower, val), 0.5f)) ? lower_pivot : pivot;
+  if (SIGNED) {
+    const float dec = Q[r];
+    if ((dec < 0.f) != (x < 0.f)) r += (x > 0.f) ? 1 : -1;
+  }
+  return static_cast<uint32_t>(r) & 0xFFu;
+}
+
+__device__ __forceinline__ bool finite_f(float g) { return fabsf(g) < __int_as_float(0x7f800000); }
+
+// Max-reduce over groups of G consecutive threads (G a power of two, <= Q_THREADS).
+template <int G>
+__device__ __forceinline__ float group_max(float v, float* red) {
+  if constexpr (G <= 32) {
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  } else {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    constexpr int WPG = G / 32;  // warps per group
+    const int g0 = (w / WPG) * WPG;
+    float r = red[g0];
+#pragma unroll
+    for (int i = 1; i < WPG; ++i) r = fmaxf(r, red[g0 + i]);
+    return r;
+  }
+}
+
+// EPT elements per thread, BS elements per quantisation block.
+template <int BS>
+__global__ __launch_bounds__(Q_THREADS) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
+  constexpr int EPT = BS > 2048 ? 16 : 8;
+  constexpr int TILE = Q_THREADS * EPT;
+  constexpr int G = BS / EPT;  // threads per quantisation block
+  __shared__ float q1[256], q2[256];
+  __shared__ float red[Q_THREADS / 32];
+  for (int i = threadIdx.x; i < 256; i += Q_THREADS) {
+    q1[i] = a.qmap1 ? a.qmap1[i] : 0.f;
+    q2[i] = a.qmap2 ? a.qmap2[i] : 0.f;
+  }
+  __syncthreads();
+  const msr_adamw8bit_hparams hp = a.hp;
+  const int64_t total = a.prefix[a.count];
+  for (int64_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    const int ei = find_entry<Q_MAXE>(a.prefix, a.count, tile);
+    const msr_adamw8bit_entry& E = a.e[ei];
+    const int64_t n = E.numel;
+    const int64_t base = (tile - a.prefix[ei]) * TILE + static_cast<int64_t>(threadIdx.x) * EPT;
+    uint16_t* P = static_cast<uint16_t*>(E.param);
+    const uint16_t* Gp = static_cast<const uint16_t*>(E.grad);
+    const bool vec = a.vec[ei] && base + EPT <= n;
+    const PhiloxKey kp = make_key(E.key_p);
+
+    uint16_t pb[EPT], gb[EPT];
+    if (vec) {
+#pragma unroll
+      for (int h = 0; h < EPT; h += 8) {
+        U16x8 t = ld_u16x8(P + base + h);
+        U16x8 u = ld_u16x8_stream(Gp + base + h);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { pb[h + j] = t.v[j]; gb[h + j] = u.v[j]; }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const bool ok = base + j < n;
+        pb[j] = ok ? P[base + j] : 0;
+        gb[j] = ok ? Gp[base + j] : 0;
+      }
+    }
+
+    float m[EPT], v[EPT];
+    if (E.quantized) {
+      const uint8_t* S1 = static_cast<const uint8_t*>(E.state1);
+      const uint8_t* S2 = static_cast<const uint8_t*>(E.state2);
+      const int64_t blk = base / BS;
+      const bool blk_ok = base < n;
+      const float am1 = blk_ok ? E.absmax1[blk] : 0.f;
+      const float am2 = blk_ok ? E.absmax2[blk] : 0.f;
+      uint8_t c1[EPT], c2[EPT];
+      if (vec) {
+#pragma unroll
+        for (int h = 0; h < EPT; h += 8) {
+          uint2 t = *reinterpret_cast<const uint2*>(S1 + base + h);
+          uint2 u = *reinterpret_cast<const uint2*>(S2 + base + h);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            c1[h + j] = (t.x >> (8 * j)) & 0xFF; c1[h + 4 + j] = (t.y >> (8 * j)) & 0xFF;
+            c2[h + j] = (u.x >> (8 * j)) & 0xFF; c2[h + 4 + j] = (u.y >> (8 * j)) & 0xFF;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          const bool ok = base + j < n;
+          c1[j] = ok ? S1[base + j] : 127;
+          c2[j] = ok ? S2[base + j] : 0;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        m[j] = fmul(q1[c1[j]], am1);
+        v[j] = fmul(q2[c2[j]], am2);
+      }
+    } else {
+      const uint16_t* S1 = static_cast<const uint16_t*>(E.state1);
+      const uint16_t* S2 = static_cast<const uint16_t*>(E.state2);
+      if (vec) {
+#pragma unroll
+        for (int h = 0; h < EPT; h += 8) {
+          U16x8 t = ld_u16x8(S1 + base + h), u = ld_u16x8(S2 + base + h);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { m[h + j] = bf16_bits_to_f32(t.v[j]); v[h + j] = bf16_bits_to_f32(u.v[j]); }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          const bool ok = base + j < n;
+          m[j] = ok ? bf16_bits_to_f32(S1[base + j]) : 0.f;
+          v[j] = ok ? bf16_bits_to_f32(S2[base + j]) : 0.f;
+        }
+      }
+    }
+
+    // Adam update (decay after the step, bitsandbytes order) -- :72-80
+    float mmax = 0.f, vmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const float g = bf16_bits_to_f32(gb[j]);
+      const bool fin = finite_f(g);
+      m[j] = fin ? fadd(fmul(hp.beta1, m[j]), fmul(hp.one_minus_beta1, g)) : 0.f;
+      v[j] = fin ? fadd(fmul(hp.beta2, v[j]), fmul(fmul(hp.one_minus_beta2, g), g)) : 0.f;
+      const float p = bf16_bits_to_f32(pb[j]);
+      const float upd = fsub(p, __fdiv_rn(fmul(E.coef, m[j]), fadd(__fsqrt_rn(v[j]), E.sqrt_bc2_eps)));
+      const float updated = fmul(upd, hp.decay);
+      if (fin) pb[j] = sr_bf16_bits(updated, philox_word0(static_cast<uint32_t>(base + j), kp));
+      if (base + j < n) {
+        mmax = fmaxf(mmax, fabsf(m[j]));
+        vmax = fmaxf(vmax, fabsf(v[j]));
+      }
+    }
+
+    if (vec) {
+#pragma unroll
+      for (int h = 0; h < EPT; h += 8) {
+        U16x8 t;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t.v[j] = pb[h + j];
+        st_u16x8(P + base + h, t);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPT; ++j)
+        if (base + j < n) P[base + j] = pb[j];
+    }
+
+    if (E.quantized) {
+      mmax = group_max<G>(mmax, red);
+      vmax = group_max<G>(vmax, red);
+      const float dm = mmax > 0.f ? mmax : 1.f;
+      const float dv = vmax > 0.f ? vmax : 1.f;
+      uint8_t* S1 = static_cast<uint8_t*>(E.state1);
+      uint8_t* S2 = static_cast<uint8_t*>(E.state2);
+      uint32_t c1w[EPT / 4], c2w[EPT / 4];
+#pragma unroll
+      for (int j = 0; j < EPT / 4; ++j) { c1w[j] = 0u; c2w[j] = 0u; }
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        c1w[j / 4] |= quantize<true>(__fdiv_rn(m[j], dm), q1) << (8 * (j % 4));
+        c2w[j / 4] |= quantize<false>(__fdiv_rn(v[j], dv), q2) << (8 * (j % 4));
+      }
+      if (vec) {
+#pragma unroll
+        for (int h = 0; h < EPT / 8; ++h) {
+          *reinterpret_cast<uint2*>(S1 + base + 8 * h) = make_uint2(c1w[2 * h], c1w[2 * h + 1]);
+          *reinterpret_cast<uint2*>(S2 + base + 8 * h) = make_uint2(c2w[2 * h], c2w[2 * h + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j)
+          if (base + j < n) {
+            S1[base + j] = (c1w[j / 4] >> (8 * (j % 4))) & 0xFF;
+            S2[base + j] = (c2w[j / 4] >> (8 * (j % 4))) & 0xFF;
+          }
+      }
+      if ((threadIdx.x % G) == 0 && base < n) {
+        E.absmax1[base / BS] = mmax;
+        E.absmax2[base / BS] = vmax;
+      }
+    } else {
+      const PhiloxKey km = make_key(E.key_m), kv = make_key(E.key_v);
+      uint16_t* S1 = static_cast<uint16_t*>(E.state1);
+      uint16_t* S2 = static_cast<uint16_t*>(E.state2);
+      uint16_t mb[EPT], vb[EPT];
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const uint32_t ctr = static_cast<uint32_t>(base + j);
+        mb[j] = sr_bf16_bits(m[j], philox_word0(ctr, km));
+        vb[j] = sr_bf16_bits(v[j], philox_word0(ctr, kv));
+      }
+      if (vec) {
+#pragma unroll
+        for (int h = 0; h < EPT; h += 8) {
+          U16x8 t, u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { t.v[j] = mb[h + j]; u.v[j] = vb[h + j]; }
+          st_u16x8(S1 + base + h, t);
+          st_u16x8(S2 + base + h, u);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j)
+          if (base + j < n) { S1[base + j] = mb[j]; S2[base + j] = vb[j]; }
+      }
+    }
+  }
+}
+
+template <int BS>
+int launch_bs(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
+  const int64_t cap = static_cast<int64_t>(sm_count()) * Q_BLOCKS_PER_SM;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
+  adamw8bit_kernel<BS><<<grid, Q_THREADS, 0, s>>>(a);
+  return check_launch("adamw8bit_kernel");
+}
+
+inline bool al(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace msr
+
+using namespace msr;
+
+extern "C" int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, const float* qmap1, const float* qmap2,
+                             const msr_adamw8bit_hparams* hp, msr_stream_t stream) {
+  if (count < 0 || (count > 0 && (entries == nullptr || hp == nullptr)))
+    return fail(MSR_ERR_INVALID, "msr_adamw8bit: bad entry list or hparams");
+  const int bs = hp->block_size;
+  if (bs < 32 || bs > 4096 || (bs & (bs - 1)))
+    return fail(MSR_ERR_INVALID, "msr_adamw8bit: block_size %d is not a power of two in [32, 4096]", bs);
+  const int ept = bs > 2048 ? 16 : 8;
+  const int64_t tile = static_cast<int64_t>(Q_THREADS) * ept;
+  for (int start = 0; start < count; start += Q_MAXE) {
+    Adam8Args a{};
+    a.hp = *hp;
+    a.qmap1 = qmap1;
+    a.qmap2 = qmap2;
+    int64_t tiles = 0;
+    bool any_quant = false;
+    for (int i = start; i < count && a.count < Q_MAXE; ++i) {
+      const msr_adamw8bit_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.grad || !e.state1 || !e.state2)))
+        return fail(MSR_ERR_INVALID, "msr_adamw8bit: entry %d has a null pointer or negative numel", i);
+      if (e.numel > 0 && e.quantized && (!e.absmax1 || !e.absmax2))
+        return fail(MSR_ERR_INVALID, "msr_adamw8bit: entry %d is quantized but has no absmax buffers", i);
+      if (e.numel == 0) continue;
+      any_quant |= e.quantized != 0;
+      a.e[a.count] = e;
+      const unsigned sa = e.quantized ? 8u : 16u;
+      a.vec[a.count] = al(e.param, 16) && al(e.grad, 16) && al(e.state1, sa) && al(e.state2, sa);
+      a.prefix[a.count] = tiles;
+      tiles += (e.numel + tile - 1) / tile;
+      ++a.count;
+    }
+    a.prefix[a.count] = tiles;
+    if (a.count == 0) continue;
+    if (any_quant && (qmap1 == nullptr || qmap2 == nullptr))
+      return fail(MSR_ERR_INVALID, "msr_adamw8bit: quantized entries need both codebooks");
+    cudaStream_t s = to_stream(stream);
+    int st;
+    switch (bs) {
+      case 32: st = launch_bs<32>(a, tiles, s); break;
+      case 64: st = launch_bs<64>(a, tiles, s); break;
+      case 128: st = launch_bs<128>(a, tiles, s); break;
+      case 256: st = launch_bs<256>(a, tiles, s); break;
+      case 512: st = launch_bs<512>(a, tiles, s); break;
+      case 1024: st = launch_bs<1024>(a, tiles, s); break;
+      case 2048: st = launch_bs<2048>(a, tiles, s); break;
+      default: st = launch_bs<4096>(a, tiles, s); break;
+    }
+    if (st) return st;
+  }
+  return MSR_OK;
+}

@@ -1,0 +1,486 @@
+// Fused elementwise kernels of the optimizer step: SR gradient accumulation, Muon
+// prepare (momentum + Nesterov), Muon apply (decay + scaled update) and AdamW-SR.
+//
+// Design (B200): multi-tensor launches. Each launch carries up to MAXE tensors in its
+// kernel parameters; the work is cut into chunks of 8192 elements that never cross a
+// tensor, and a persistent grid (a multiple of the SM count) walks the chunks. Each thread
+// moves 8 bf16 per 16-byte access, issuing all loads of a chunk before its math so that
+// every SM keeps enough bytes in flight for HBM3e. All fp32 arithmetic uses explicit
+// round-to-nearest intrinsics (no contraction into FMA), in the reference's op order, so
+// results are bit-identical to the reference kernels' fp32 evaluation.
+#include "common.cuh"
+#include "host_common.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace msr {
+namespace {
+
+constexpr int EW_THREADS = 256;
+constexpr int EW_VEC = 8;
+constexpr int EW_ITERS = 4;
+constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 8192 elements
+constexpr int MAXE = 64;
+constexpr int EW_BLOCKS_PER_SM = 4;
+
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+
+// ---------------------------------------------------------------------------------------
+// Philox test hook
+// ---------------------------------------------------------------------------------------
+__global__ void philox_fill_kernel(uint32_t* out, int64_t n, uint64_t ctr_base, PhiloxKey key) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = philox_word0(static_cast<uint32_t>(ctr_base + static_cast<uint64_t>(i)), key);
+}
+
+// ---------------------------------------------------------------------------------------
+// SR gradient accumulation: acc <- SR(acc + g) -- muon_sr/triton_adamw.py:206-229
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint16_t accum_one(uint16_t a, uint16_t g, uint32_t ctr, PhiloxKey key) {
+  const float s = fadd(bf16_bits_to_f32(a), bf16_bits_to_f32(g));
+  return sr_bf16_bits(s, philox_word0(ctr, key));
+}
+
+// First micro-batch: SR(0 + g) == g exactly (g is already bf16), except -0 + 0 = +0.
+__device__ __forceinline__ uint16_t first_one(uint16_t g) { return g == 0x8000u ? uint16_t(0) : g; }
+
+template <bool VEC>
+__global__ __launch_bounds__(EW_THREADS) void grad_accum_first_kernel(uint16_t* __restrict__ acc,
+                                                                     const uint16_t* __restrict__ g, int64_t n) {
+  const int64_t nvec = VEC ? n / EW_VEC : 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    U16x8 v = ld_u16x8_stream(g + i * EW_VEC);
+#pragma unroll
+    for (int j = 0; j < EW_VEC; ++j) v.v[j] = first_one(v.v[j]);
+    st_u16x8(acc + i * EW_VEC, v);
+  }
+  for (int64_t i = nvec * EW_VEC + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    acc[i] = first_one(g[i]);
+}
+
+template <bool VEC>
+__global__ __launch_bounds__(EW_THREADS) void grad_accum_kernel(uint16_t* __restrict__ acc,
+                                                               const uint16_t* __restrict__ g,
+                                                               int64_t n, PhiloxKey key) {
+  const int64_t nchunks = (n + EW_CHUNK - 1) / EW_CHUNK;
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const int64_t base = chunk * EW_CHUNK;
+    if (VEC) {
+      U16x8 va[EW_ITERS], vg[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          va[it] = ld_u16x8(acc + idx);
+          vg[it] = ld_u16x8_stream(g + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 o;
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            o.v[j] = accum_one(va[it].v[j], vg[it].v[j], static_cast<uint32_t>(idx + j), key);
+          st_u16x8(acc + idx, o);
+        } else {
+          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one(acc[i], g[i], static_cast<uint32_t>(i), key);
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) acc[i] = accum_one(acc[i], g[i], static_cast<uint32_t>(i), key);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Muon prepare -- muon_sr/triton_muon_sr.py:18-50
+// ---------------------------------------------------------------------------------------
+struct PrepareArgs {
+  msr_prepare_entry e[MAXE];
+  int64_t prefix[MAXE + 1];
+  uint8_t vec[MAXE];
+  int count;
+  float beta, omb;
+  int nesterov;
+};
+
+__device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, float beta, float omb, bool nesterov,
+                                            uint32_t ctr, PhiloxKey key, uint16_t& buf_out, uint16_t& upd_out,
+                                            float& nsq) {
+  const float g = bf16_bits_to_f32(g_bits);
+  const float buf = bf16_bits_to_f32(b_bits);
+  const float nb = fadd(buf, fmul(omb, fsub(g, buf)));
+  const float upd = nesterov ? fadd(g, fmul(beta, fsub(nb, g))) : nb;
+  buf_out = sr_bf16_bits(nb, philox_word0(ctr, key));
+  upd_out = rne_bf16_bits(upd);
+  const float r = bf16_bits_to_f32(upd_out);
+  nsq = fmaf(r, r, nsq);
+}
+
+__device__ __forceinline__ float block_sum(float v) {
+  __shared__ float red[EW_THREADS / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x == 0)
+    for (int i = 0; i < EW_THREADS / 32; ++i) s += red[i];
+  return s;
+}
+
+__global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
+  const int64_t total = a.prefix[a.count];
+  const bool nesterov = a.nesterov != 0;
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_prepare_entry& E = a.e[ei];
+    const uint16_t* g = static_cast<const uint16_t*>(E.grad);
+    uint16_t* mb = static_cast<uint16_t*>(E.momentum);
+    uint16_t* up = static_cast<uint16_t*>(E.update);
+    const int64_t n = E.numel;
+    const PhiloxKey key = make_key(E.key);
+    const uint64_t cb = E.ctr_base;
+    const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
+    float nsq = 0.f;
+    if (a.vec[ei]) {
+      U16x8 vg[EW_ITERS], vb[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vg[it] = ld_u16x8_stream(g + idx);
+          vb[it] = ld_u16x8(mb + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 ob, ou;
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            prepare_one(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
+                        static_cast<uint32_t>(cb + static_cast<uint64_t>(idx + j)), key, ob.v[j], ou.v[j], nsq);
+          st_u16x8(mb + idx, ob);
+          st_u16x8(up + idx, ou);
+        } else {
+          for (int64_t i = idx; i < n; ++i) {
+            uint16_t ob, ou;
+            prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
+                        ob, ou, nsq);
+            mb[i] = ob;
+            up[i] = ou;
+          }
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) {
+          uint16_t ob, ou;
+          prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
+                      ob, ou, nsq);
+          mb[i] = ob;
+          up[i] = ou;
+        }
+      }
+    }
+    if (E.norm_sq != nullptr) {
+      const float s = block_sum(nsq);
+      if (threadIdx.x == 0) atomicAdd(E.norm_sq, s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Muon apply -- muon_sr/triton_muon_sr.py:53-80
+// ---------------------------------------------------------------------------------------
+struct ApplyArgs {
+  msr_apply_entry e[MAXE];
+  int64_t prefix[MAXE + 1];
+  uint8_t vec[MAXE];
+  int count;
+  float lr, decay;
+};
+
+__device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, float scale, float lr, float decay,
+                                              uint32_t ctr, PhiloxKey key) {
+  const float u = fmul(bf16_bits_to_f32(u_bits), scale);
+  float p = fmul(bf16_bits_to_f32(p_bits), decay);
+  p = fsub(p, fmul(lr, u));
+  return sr_bf16_bits(p, philox_word0(ctr, key));
+}
+
+__global__ __launch_bounds__(EW_THREADS) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
+  const int64_t total = a.prefix[a.count];
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_apply_entry& E = a.e[ei];
+    uint16_t* p = static_cast<uint16_t*>(E.param);
+    const uint16_t* u = static_cast<const uint16_t*>(E.update);
+    const int64_t n = E.numel;
+    const PhiloxKey key = make_key(E.key);
+    const float scale = E.scale;
+    const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
+    if (a.vec[ei]) {
+      U16x8 vp[EW_ITERS], vu[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vp[it] = ld_u16x8(p + idx);
+          vu[it] = ld_u16x8_stream(u + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 o;
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            o.v[j] = apply_one(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay, static_cast<uint32_t>(idx + j), key);
+          st_u16x8(p + idx, o);
+        } else {
+          for (int64_t i = idx; i < n; ++i) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, static_cast<uint32_t>(i), key);
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, static_cast<uint32_t>(i), key);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// AdamW-SR -- muon_sr/triton_adamw.py:9-72
+// ---------------------------------------------------------------------------------------
+struct AdamWArgs {
+  msr_adamw_entry e[MAXE];
+  int64_t prefix[MAXE + 1];
+  uint8_t vec[MAXE];
+  int count;
+  msr_adamw_hparams hp;
+};
+
+__device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uint16_t& m_bits, uint16_t& v_bits,
+                                          const msr_adamw_hparams& hp, float step_size, float bc2s, uint32_t ctr,
+                                          PhiloxKey km, PhiloxKey kv, PhiloxKey kp) {
+  const float g = bf16_bits_to_f32(g_bits);
+  float m = bf16_bits_to_f32(m_bits);
+  float v = bf16_bits_to_f32(v_bits);
+  float p = bf16_bits_to_f32(p_bits);
+  m = fadd(fmul(hp.beta1, m), fmul(hp.one_minus_beta1, g));
+  v = fadd(fmul(hp.beta2, v), fmul(fmul(hp.one_minus_beta2, g), g));
+  const float denom = fadd(__fdiv_rn(__fsqrt_rn(v), bc2s), hp.eps);
+  p = fmul(p, hp.decay);
+  p = fsub(p, __fdiv_rn(fmul(step_size, m), denom));
+  m_bits = sr_bf16_bits(m, philox_word0(ctr, km));
+  v_bits = sr_bf16_bits(v, philox_word0(ctr, kv));
+  p_bits = sr_bf16_bits(p, philox_word0(ctr, kp));
+}
+
+__global__ __launch_bounds__(EW_THREADS) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
+  const int64_t total = a.prefix[a.count];
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_adamw_entry& E = a.e[ei];
+    uint16_t* p = static_cast<uint16_t*>(E.param);
+    const uint16_t* g = static_cast<const uint16_t*>(E.grad);
+    uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
+    uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
+    const int64_t n = E.numel;
+    const PhiloxKey km = make_key(E.key_m), kv = make_key(E.key_v), kp = make_key(E.key_p);
+    const float ss = E.step_size, bc2s = E.bc2_sqrt;
+    const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
+    if (a.vec[ei]) {
+      U16x8 vp[EW_ITERS], vg[EW_ITERS], vm[EW_ITERS], vv[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vp[it] = ld_u16x8(p + idx);
+          vg[it] = ld_u16x8_stream(g + idx);
+          vm[it] = ld_u16x8(m + idx);
+          vv[it] = ld_u16x8(v + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            adamw_one(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s,
+                      static_cast<uint32_t>(idx + j), km, kv, kp);
+          st_u16x8(p + idx, vp[it]);
+          st_u16x8(m + idx, vm[it]);
+          st_u16x8(v + idx, vv[it]);
+        } else {
+          for (int64_t i = idx; i < n; ++i) {
+            uint16_t pb = p[i], mb = m[i], vb = v[i];
+            adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, static_cast<uint32_t>(i), km, kv, kp);
+            p[i] = pb; m[i] = mb; v[i] = vb;
+          }
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) {
+          uint16_t pb = p[i], mb = m[i], vb = v[i];
+          adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, static_cast<uint32_t>(i), km, kv, kp);
+          p[i] = pb; m[i] = mb; v[i] = vb;
+        }
+      }
+    }
+  }
+}
+
+inline bool ptr_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int grid_for(int64_t chunks) {
+  const int64_t cap = static_cast<int64_t>(sm_count()) * EW_BLOCKS_PER_SM;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(chunks, cap)));
+}
+
+}  // namespace
+}  // namespace msr
+
+using namespace msr;
+
+extern "C" {
+
+int msr_philox_fill(uint32_t* out, int64_t n, uint64_t ctr_base, uint64_t key, msr_stream_t stream) {
+  if (n < 0 || (n > 0 && out == nullptr)) return fail(MSR_ERR_INVALID, "msr_philox_fill: bad arguments");
+  if (n == 0) return MSR_OK;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+  philox_fill_kernel<<<blocks, 256, 0, to_stream(stream)>>>(out, n, ctr_base, make_key(key));
+  return check_launch("philox_fill_kernel");
+}
+
+int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, int first, msr_stream_t stream) {
+  if (n < 0 || (n > 0 && (acc == nullptr || grad == nullptr)))
+    return fail(MSR_ERR_INVALID, "msr_grad_accum_bf16: null pointer or negative size");
+  if (n == 0) return MSR_OK;
+  const int64_t chunks = (n + EW_CHUNK - 1) / EW_CHUNK;
+  const bool vec = ptr_aligned16(acc) && ptr_aligned16(grad);
+  if (first) {
+    const int grid = grid_for(chunks * 4);
+    if (vec)
+      grad_accum_first_kernel<true><<<grid, EW_THREADS, 0, to_stream(stream)>>>(
+          static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
+    else
+      grad_accum_first_kernel<false><<<grid, EW_THREADS, 0, to_stream(stream)>>>(
+          static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
+    return check_launch("grad_accum_first_kernel");
+  }
+  if (vec)
+    grad_accum_kernel<true><<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(
+        static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n, make_key(key));
+  else
+    grad_accum_kernel<false><<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(
+        static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n, make_key(key));
+  return check_launch("grad_accum_kernel");
+}
+
+int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta, int nesterov,
+                     msr_stream_t stream) {
+  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_prepare: bad entry list");
+  for (int start = 0; start < count; start += MAXE) {
+    PrepareArgs a{};
+    a.count = 0;
+    a.beta = beta;
+    a.omb = one_minus_beta;
+    a.nesterov = nesterov;
+    int64_t chunks = 0;
+    for (int i = start; i < count && a.count < MAXE; ++i) {
+      const msr_prepare_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.grad || !e.momentum || !e.update)))
+        return fail(MSR_ERR_INVALID, "msr_muon_prepare: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.vec[a.count] = ptr_aligned16(e.grad) && ptr_aligned16(e.momentum) && ptr_aligned16(e.update);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
+      ++a.count;
+    }
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    muon_prepare_kernel<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_prepare_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
+int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float decay, msr_stream_t stream) {
+  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_apply: bad entry list");
+  for (int start = 0; start < count; start += MAXE) {
+    ApplyArgs a{};
+    a.lr = lr;
+    a.decay = decay;
+    int64_t chunks = 0;
+    for (int i = start; i < count && a.count < MAXE; ++i) {
+      const msr_apply_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.update)))
+        return fail(MSR_ERR_INVALID, "msr_muon_apply: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.update);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
+      ++a.count;
+    }
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    muon_apply_kernel<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_apply_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
+int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp, msr_stream_t stream) {
+  if (count < 0 || (count > 0 && (entries == nullptr || hp == nullptr)))
+    return fail(MSR_ERR_INVALID, "msr_adamw_sr: bad entry list or hparams");
+  for (int start = 0; start < count; start += MAXE) {
+    AdamWArgs a{};
+    a.hp = *hp;
+    int64_t chunks = 0;
+    for (int i = start; i < count && a.count < MAXE; ++i) {
+      const msr_adamw_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.grad || !e.exp_avg || !e.exp_avg_sq)))
+        return fail(MSR_ERR_INVALID, "msr_adamw_sr: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.grad) && ptr_aligned16(e.exp_avg) &&
+                       ptr_aligned16(e.exp_avg_sq);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
+      ++a.count;
+    }
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    adamw_kernel<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("adamw_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
+}  // extern "C"

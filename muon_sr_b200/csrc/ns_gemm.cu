@@ -1,0 +1,570 @@
+// Newton-Schulz on the B200 tensor cores: a persistent, warp-specialised tcgen05 GEMM with
+// TMA-fed shared-memory stages, fp32 accumulators in TMEM and the Newton-Schulz epilogue
+// (alpha * acc + beta * C, per-matrix scale) fused into the TMEM read-back.
+//
+// Replaces _newton_schulz (muon_sr/muon_sr.py:82-98), which the reference runs as torch
+// bf16 matmuls (cuBLAS on the GPU) with a separate elementwise op for every term.
+//
+// Kernel layout (one CTA per SM, 256 threads):
+//   warp 0      TMA producer: streams A and B k-blocks (64 deep) into a 4-stage ring
+//   warp 1      TMEM allocator and MMA issuer (one thread issues tcgen05.mma 128x256x16)
+//   warps 4..7  epilogue: tcgen05.ld of the accumulator (lane quarter = warp % 4),
+//               alpha/beta/scale, RNE to bf16, 16-byte global stores
+// Two 256-column fp32 accumulators (all 512 TMEM columns) let the epilogue of one tile run
+// under the main loop of the next. Operands are either K-major or MN-major (descriptor bit),
+// which covers X X^T, A A and B X for both orientations of X without any transposes.
+// Every barrier wait has a time limit; on expiry the CTA records an error, drains what it
+// has in flight, frees TMEM and returns.
+#include "common.cuh"
+#include "host_common.h"
+#include "tc.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace msr {
+
+__device__ int g_msr_device_error = 0;
+
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, UMMA_K = 16;
+constexpr int NUM_THREADS = 256;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // 1 s: far above any legitimate wait
+
+// Error codes recorded in g_msr_device_error (role of the wait that expired).
+constexpr int ERR_TMA_WAIT = 0x101, ERR_MMA_WAIT = 0x102, ERR_EPI_WAIT = 0x103;
+
+struct SharedStorage {
+  alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Params {
+  int64_t M, N, K, batch;
+  int64_t tiles_m, tiles_n, num_tiles;
+  uint16_t* d;
+  const uint16_t* c;
+  int64_t ldd, ldc, d_bstride, c_bstride;
+  float alpha, beta;
+  const float* scale;      // per matrix; interpreted as ||x||_F^2 when scale_is_norm_sq
+  int alpha_pow, beta_pow, scale_is_norm_sq;
+};
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
+
+template <int A_MN, int B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  SharedStorage& S = *reinterpret_cast<SharedStorage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort = &S.abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&S.full[s], 1);
+      tc::mbar_init(&S.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&S.tmem_full[a], 1);
+      tc::mbar_init(&S.tmem_empty[a], 128);
+    }
+    tc::mbar_init(&S.drain, 1);
+    S.abort = 0;
+    tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tmA);
+    tc::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&S.tmem_base, TMEM_COLS);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+  }
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem_base = S.tmem_base;
+  const int64_t num_kb = (p.K + BK - 1) / BK;
+  const int64_t tiles_per_batch = p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_parity = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const int32_t b = static_cast<int32_t>(t / tiles_per_batch);
+        const int64_t r = t % tiles_per_batch;
+        const int32_t m0 = static_cast<int32_t>((r / p.tiles_n) * BM);
+        const int32_t n0 = static_cast<int32_t>((r % p.tiles_n) * BN);
+        for (int64_t kb = 0; kb < num_kb; ++kb) {
+          if (!tc::mbar_wait(&S.empty[stage], phase ^ 1u, abort, WAIT_LIMIT_NS)) {
+            record_error(ERR_TMA_WAIT);
+            ok = false;
+            break;
+          }
+          uint8_t* sa = S.stage[stage];
+          uint8_t* sb = S.stage[stage] + A_BYTES;
+          const int32_t k0 = static_cast<int32_t>(kb * BK);
+          tc::mbar_arrive_expect_tx(&S.full[stage], STAGE_BYTES);
+          if (A_MN) {
+            tc::tma_load_3d(sa, &tmA, &S.full[stage], m0, k0, b);
+            tc::tma_load_3d(sa + 8192, &tmA, &S.full[stage], m0 + 64, k0, b);
+          } else {
+            tc::tma_load_3d(sa, &tmA, &S.full[stage], k0, m0, b);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tc::tma_load_3d(sb + 8192 * i, &tmB, &S.full[stage], n0 + 64 * i, k0, b);
+          } else {
+            tc::tma_load_3d(sb, &tmB, &S.full[stage], k0, n0, b);
+          }
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Give up: let every copy already issued land before the CTA's shared memory goes.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s)) {
+            volatile int no_abort = 0;
+            tc::mbar_wait(&S.full[s], (last_parity >> s) & 1u, &no_abort, WAIT_LIMIT_NS);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!tc::mbar_wait(&S.tmem_empty[acc], acc_phase ^ 1u, abort, WAIT_LIMIT_NS)) {
+          record_error(ERR_MMA_WAIT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int64_t kb = 0; kb < num_kb; ++kb) {
+          if (!tc::mbar_wait(&S.full[stage], phase, abort, WAIT_LIMIT_NS)) {
+            record_error(ERR_MMA_WAIT);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sa = tc::smem_addr(S.stage[stage]);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint32_t aoff = A_MN ? static_cast<uint32_t>(k * UMMA_K * 128) : static_cast<uint32_t>(k * UMMA_K * 2);
+            const uint32_t boff = B_MN ? static_cast<uint32_t>(k * UMMA_K * 128) : static_cast<uint32_t>(k * UMMA_K * 2);
+            const uint64_t adesc = tc::smem_desc_sw128(sa + aoff, a_lbo, 1024u);
+            const uint64_t bdesc = tc::smem_desc_sw128(sb + boff, b_lbo, 1024u);
+            tc::mma_bf16(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc::mma_commit(&S.tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued above has finished before TMEM can be released.
+      tc::mma_commit(&S.drain);
+      volatile int no_abort = 0;
+      tc::mbar_wait(&S.drain, 0, &no_abort, WAIT_LIMIT_NS);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      if (!tc::mbar_wait(&S.tmem_full[acc], acc_phase, abort, WAIT_LIMIT_NS)) {
+        record_error(ERR_EPI_WAIT);
+        break;
+      }
+      tc::fence_after_sync();
+      const int64_t b = t / tiles_per_batch;
+      const int64_t r = t % tiles_per_batch;
+      const int64_t m0 = (r / p.tiles_n) * BM;
+      const int64_t n0 = (r % p.tiles_n) * BN;
+      float alpha = p.alpha, beta = p.beta;
+      if (p.scale != nullptr) {
+        float s = p.scale[b];
+        if (p.scale_is_norm_sq) s = 1.0f / (sqrtf(s) + 1e-7f);
+        if (p.alpha_pow == 1) alpha *= s; else if (p.alpha_pow == 2) alpha *= s * s;
+        if (p.beta_pow == 1) beta *= s;
+      }
+      const int64_t row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      uint16_t* drow = p.d + b * p.d_bstride + row * p.ldd;
+      const uint16_t* crow = p.c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        // tcgen05.ld is warp-collective: every lane issues it, converged, then masks.
+        __syncwarp();
+        uint32_t v[32];
+        tc::tmem_ld_32x32b_x32(tbase + cc * 32, v);
+        tc::tmem_ld_wait();
+        const int64_t col0 = n0 + cc * 32;
+        if (row_ok && col0 < p.N) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int64_t col = col0 + g * 8;
+            if (col < p.N) {
+              float cin[8];
+              const bool full = col + 8 <= p.N;
+              if (crow != nullptr && beta != 0.f) {
+                if (full) {
+                  const U16x8 cv = ld_u16x8(crow + col);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) cin[j] = bf16_bits_to_f32(cv.v[j]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) cin[j] = (col + j < p.N) ? bf16_bits_to_f32(crow[col + j]) : 0.f;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cin[j] = 0.f;
+              }
+              U16x8 o;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float accv = __uint_as_float(v[g * 8 + j]);
+                o.v[j] = rne_bf16_bits(fmaf(alpha, accv, beta * cin[j]));
+              }
+              if (full) {
+                st_u16x8(drow + col, o);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  if (col + j < p.N) drow[col + j] = o.v[j];
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      tc::fence_before_sync();
+      tc::mbar_arrive(&S.tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side: tensor maps and launches
+// ---------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map over [batch][outer][inner] (inner contiguous), box {64, box_outer, 1},
+// 128-byte swizzle, zero fill outside the tensor.
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t batch, int64_t batch_stride_elems,
+             uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(MSR_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner) * 2, static_cast<cuuint64_t>(batch_stride_elems) * 2};
+  cuuint32_t box[3] = {64u, box_outer, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MSR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for inner=%lld outer=%lld batch=%lld", (int)r,
+                (long long)inner, (long long)outer, (long long)batch);
+  return MSR_OK;
+}
+
+size_t smem_bytes() { return sizeof(SharedStorage) + 1024; }
+
+template <int A_MN, int B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
+  auto kern = gemm_kernel<A_MN, B_MN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, sm_count()));
+  kern<<<grid, NUM_THREADS, smem_bytes(), s>>>(ta, tb, p);
+  return check_launch("gemm_kernel");
+}
+
+// D[b] = alpha_b * op(A)[b] x op(B)[b]^T + beta_b * C[b]. A K-major: [batch][M][K]; MN-major:
+// [batch][K][M]. B K-major: [batch][N][K]; MN-major: [batch][K][N]. C, D: [batch][M][N] with
+// row strides ldc, ldd.
+int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn, int64_t b_bstride, const void* c,
+         int64_t ldc, int64_t c_bstride, void* d, int64_t ldd, int64_t d_bstride, int64_t batch, int64_t M, int64_t N,
+         int64_t K, float alpha, float beta, const float* scale, int alpha_pow, int beta_pow, int scale_is_norm_sq,
+         cudaStream_t s) {
+  CUtensorMap ta, tb;
+  int st = a_mn ? make_map(&ta, a, M, K, batch, a_bstride, 64) : make_map(&ta, a, K, M, batch, a_bstride, BM);
+  if (st) return st;
+  st = b_mn ? make_map(&tb, b, N, K, batch, b_bstride, 64) : make_map(&tb, b, K, N, batch, b_bstride, BN);
+  if (st) return st;
+  Params p{};
+  p.M = M; p.N = N; p.K = K; p.batch = batch;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.num_tiles = p.tiles_m * p.tiles_n * batch;
+  p.d = static_cast<uint16_t*>(d);
+  p.c = static_cast<const uint16_t*>(c);
+  p.ldd = ldd; p.ldc = ldc; p.d_bstride = d_bstride; p.c_bstride = c_bstride;
+  p.alpha = alpha; p.beta = beta;
+  p.scale = scale; p.alpha_pow = alpha_pow; p.beta_pow = beta_pow; p.scale_is_norm_sq = scale_is_norm_sq;
+  if (a_mn && b_mn) return launch<1, 1>(ta, tb, p, s);
+  if (a_mn) return launch<1, 0>(ta, tb, p, s);
+  if (b_mn) return launch<0, 1>(ta, tb, p, s);
+  return launch<0, 0>(ta, tb, p, s);
+}
+
+// ---------------------------------------------------------------------------------------
+// Small helper kernels of the Newton-Schulz driver
+// ---------------------------------------------------------------------------------------
+// norm_sq[b] += sum of squares of x[b] (caller zeroes norm_sq).
+__global__ void norm_sq_kernel(const uint16_t* __restrict__ x, int64_t per, float* __restrict__ out) {
+  const int64_t b = blockIdx.y;
+  const uint16_t* xb = x + b * per;
+  float s = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = bf16_bits_to_f32(xb[i]);
+    s = fmaf(v, v, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    atomicAdd(out + b, t);
+  }
+}
+
+// dst[b][r][c] (dst dims R2 x C2) = src[b][r][c] for r < R, c < C, else 0 -- or the reverse copy.
+__global__ void pad_copy_kernel(const uint16_t* __restrict__ src, int64_t sR, int64_t sC, uint16_t* __restrict__ dst,
+                                int64_t dR, int64_t dC, int64_t batch) {
+  const int64_t total = batch * dR * dC;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % dC;
+    const int64_t r = (i / dC) % dR;
+    const int64_t b = i / (dC * dR);
+    dst[i] = (r < sR && c < sC) ? src[(b * sR + r) * sC + c] : uint16_t(0);
+  }
+}
+
+// out = RNE(x * 1/(||x||+1e-7)): Newton-Schulz with zero steps.
+__global__ void scale_copy_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ out, int64_t per,
+                                  int64_t batch, const float* __restrict__ nsq) {
+  const int64_t total = per * batch;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = 1.0f / (sqrtf(nsq[i / per]) + 1e-7f);
+    out[i] = rne_bf16_bits(bf16_bits_to_f32(x[i]) * s);
+  }
+}
+
+inline int64_t round8(int64_t v) { return (v + 7) / 8 * 8; }
+inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct NsLayout {
+  bool padded, transposed;
+  int64_t R8, C8, m, n;
+  size_t off_nsq, off_a, off_b, off_w1, off_w2, off_pin, total;
+};
+
+NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
+  NsLayout L{};
+  L.transposed = rows > cols;
+  L.R8 = round8(rows);
+  L.C8 = round8(cols);
+  L.padded = (L.R8 != rows) || (L.C8 != cols);
+  L.m = L.transposed ? L.C8 : L.R8;
+  L.n = L.transposed ? L.R8 : L.C8;
+  const size_t xb = static_cast<size_t>(batch) * L.R8 * L.C8 * 2;
+  const size_t gb = static_cast<size_t>(batch) * L.m * L.m * 2;
+  size_t o = 0;
+  L.off_nsq = o; o = align256(o + static_cast<size_t>(batch) * 4);
+  L.off_a = o;   o = align256(o + gb);
+  L.off_b = o;   o = align256(o + gb);
+  L.off_w1 = o;  o = align256(o + xb);
+  L.off_w2 = o;  if (L.padded) o = align256(o + xb);
+  L.off_pin = o; if (L.padded) o = align256(o + xb);
+  L.total = o;
+  return L;
+}
+
+}  // namespace gemm
+}  // namespace msr
+
+using namespace msr;
+using namespace msr::gemm;
+
+extern "C" {
+
+int msr_device_error(msr_stream_t stream, int clear) {
+  cudaError_t e = cudaStreamSynchronize(to_stream(stream));
+  if (e != cudaSuccess) return fail(-1, "cudaStreamSynchronize: %s", cudaGetErrorString(e)), -1;
+  int value = 0;
+  e = cudaMemcpyFromSymbol(&value, g_msr_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail(-1, "read device error: %s", cudaGetErrorString(e)), -1;
+  if (clear && value != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_msr_device_error, &zero, sizeof(int));
+  }
+  return value;
+}
+
+int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c, void* d, int64_t batch,
+                  int64_t M, int64_t N, int64_t K, float alpha, float beta, const float* scale, int alpha_pow,
+                  int beta_pow, msr_stream_t stream) {
+  if (!a || !b || !d || batch <= 0 || M <= 0 || N <= 0 || K <= 0)
+    return fail(MSR_ERR_INVALID, "msr_gemm_bf16: null pointer or non-positive size");
+  const int64_t a_inner = a_mn_major ? M : K, b_inner = b_mn_major ? N : K;
+  if (a_inner % 8 || b_inner % 8 || N % 8)
+    return fail(MSR_ERR_INVALID, "msr_gemm_bf16: contiguous dims must be multiples of 8 (got A %lld, B %lld, N %lld)",
+                (long long)a_inner, (long long)b_inner, (long long)N);
+  if (int st = require_sm100()) return st;
+  return run_gemm(a, a_mn_major, M * K, b, b_mn_major, N * K, c, N, M * N, d, N, M * N, batch, M, N, K, alpha, beta, scale,
+              alpha_pow, beta_pow, 0, to_stream(stream));
+}
+
+size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return ns_layout(batch, rows, cols).total;
+}
+
+int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols, int steps,
+                           const float* norm_sq, void* workspace, size_t workspace_bytes, msr_stream_t stream) {
+  if (!x || !out || batch <= 0 || rows <= 0 || cols <= 0 || steps < 0)
+    return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: null pointer or bad size");
+  if (x == out) return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: out must not alias x");
+  const NsLayout L = ns_layout(batch, rows, cols);
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(MSR_ERR_WORKSPACE, "msr_newton_schulz_bf16: workspace %zu < %zu bytes", workspace_bytes, L.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || reinterpret_cast<uintptr_t>(x) % 16 ||
+      reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: x/out must be 16-byte and workspace 256-byte aligned");
+  if (int st = require_sm100()) return st;
+  cudaStream_t s = to_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t per = rows * cols;
+
+  const float* nsq = norm_sq;
+  if (nsq == nullptr) {
+    float* t = reinterpret_cast<float*>(ws + L.off_nsq);
+    cudaMemsetAsync(t, 0, static_cast<size_t>(batch) * 4, s);
+    const int gx = static_cast<int>(std::min<int64_t>((per + 255) / 256, std::max<int64_t>(1, 4 * sm_count() / batch + 1)));
+    norm_sq_kernel<<<dim3(gx, static_cast<unsigned>(batch)), 256, 0, s>>>(static_cast<const uint16_t*>(x), per, t);
+    if (int st = check_launch("norm_sq_kernel")) return st;
+    nsq = t;
+  }
+  const int ew_grid = 4 * sm_count();
+  if (steps == 0) {
+    scale_copy_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), per, batch, nsq);
+    return check_launch("scale_copy_kernel");
+  }
+
+  const int64_t R = L.R8, C = L.C8, m = L.m, n = L.n;
+  const int64_t xs = R * C, gs = m * m;
+  uint16_t* A = reinterpret_cast<uint16_t*>(ws + L.off_a);
+  uint16_t* B = reinterpret_cast<uint16_t*>(ws + L.off_b);
+  const uint16_t* src;
+  uint16_t* bufs[2];
+  if (L.padded) {
+    uint16_t* pin = reinterpret_cast<uint16_t*>(ws + L.off_pin);
+    pad_copy_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, pin, R, C, batch);
+    if (int st = check_launch("pad_copy_kernel")) return st;
+    src = pin;
+    bufs[0] = reinterpret_cast<uint16_t*>(ws + L.off_w1);
+    bufs[1] = reinterpret_cast<uint16_t*>(ws + L.off_w2);
+  } else {
+    src = static_cast<const uint16_t*>(x);
+    // Step s writes bufs[(steps - 1 - s) & 1] so that the last step lands in `out`.
+    bufs[0] = static_cast<uint16_t*>(out);
+    bufs[1] = reinterpret_cast<uint16_t*>(ws + L.off_w1);
+  }
+  const float a_ = 3.4445f, b_ = -4.7750f, c_ = 2.0315f;
+  for (int st_i = 0; st_i < steps; ++st_i) {
+    uint16_t* dst = L.padded ? bufs[st_i & 1] : bufs[(steps - 1 - st_i) & 1];
+    const float* sc = st_i == 0 ? nsq : nullptr;
+    int st;
+    // A = X X^T (wide orientation): K-major X rows, or MN-major columns of a tall X.
+    if (!L.transposed)
+      st = run_gemm(src, 0, xs, src, 0, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, s);
+    else
+      st = run_gemm(src, 1, xs, src, 1, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, s);
+    if (st) return st;
+    // B = c (A A) + b A   (A symmetric: A A = A A^T)
+    st = run_gemm(A, 0, gs, A, 0, gs, A, m, gs, B, m, gs, batch, m, m, m, c_, b_, nullptr, 0, 0, 0, s);
+    if (st) return st;
+    // X' = B X + a X  (tall X: X' = X B + a X with B symmetric)
+    if (!L.transposed)
+      st = run_gemm(B, 0, gs, src, 1, xs, src, C, xs, dst, C, xs, batch, m, n, m, 1.f, a_, sc, 1, 1, 1, s);
+    else
+      st = run_gemm(src, 0, xs, B, 0, gs, src, C, xs, dst, C, xs, batch, R, C, C, 1.f, a_, sc, 1, 1, 1, s);
+    if (st) return st;
+    src = dst;
+  }
+  if (L.padded) {
+    pad_copy_kernel<<<ew_grid, 256, 0, s>>>(src, R, C, static_cast<uint16_t*>(out), rows, cols, batch);
+    return check_launch("pad_copy_kernel (out)");
+  }
+  return MSR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,354 @@
+"""Muon with BF16 stochastic rounding on the B200 engine.
+
+Public classes keep the reference's names, constructor signatures, param-group keys, state
+keys and seed formulas (muon_sr/triton_muon_sr.py:180-373, muon_sr/muon_sr.py:234-418):
+
+* ``TritonMuonSR``, ``TritonMuonSRWithAuxAdam`` -- deterministic seeds from (step, index).
+* ``MuonSR``, ``MuonSRWithAuxAdam`` -- the reference's pure-PyTorch variants; here they run
+  on the same CUDA kernels with seeds drawn from torch's default generator (the reference
+  draws its rounding noise with ``torch.randint_like``), and keep those classes' state keys.
+
+Every step is: a multi-tensor prepare kernel (momentum, Nesterov, SR momentum, RNE update,
+per-matrix squared Frobenius norm), the tcgen05 Newton-Schulz chain over each shape stack,
+and a multi-tensor apply kernel (decay, scaled update, SR weights). ``shard`` (optional)
+spreads the matrices over the ranks of a process group (see ``sharding``).
+"""
+from collections import defaultdict
+
+import torch
+from torch.optim import Optimizer
+
+from . import kernels as K
+from .seeds import deterministic_seed
+
+# Max elements per batched Newton-Schulz call, as in the reference (triton_muon_sr.py:125).
+# Each matrix is computed independently, so results do not depend on the chunking.
+NS_CHUNK_NUMEL = 1 << 28
+
+
+def _restore_global_step(state, groups):
+    """muon_sr/triton_muon_sr.py:13-15."""
+    return max((state[p].get("step", 0) for g in groups for p in g["params"]), default=0)
+
+
+def _init_stacked_bufs(params, device, state):
+    """One bf16 [N, *shape] momentum stack per distinct shape; ``state[p]["momentum_buffer"]``
+    is a view into it (muon_sr/muon_sr.py:112-146)."""
+    shape_groups = defaultdict(list)
+    for p in params:
+        shape_groups[p.shape].append(p)
+    stacked_bufs, buf_indices = {}, {}
+    for shape, grp in shape_groups.items():
+        stacked = torch.zeros(len(grp), *shape, dtype=torch.bfloat16, device=device)
+        for i, p in enumerate(grp):
+            buf_indices[id(p)] = i
+            p_state = state[p]
+            if "momentum_buffer" in p_state:
+                stacked[i].copy_(p_state["momentum_buffer"])
+            p_state["momentum_buffer"] = stacked[i]
+        stacked_bufs[shape] = stacked
+    return dict(shape_groups), stacked_bufs, buf_indices
+
+
+class _StackedBufsMixin:
+    """Stacked buffers and the global step live outside ``self.state``; rebuild them from
+    the loaded state on the next step (muon_sr/muon_sr.py:149-158)."""
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        self._batch_state = {}
+        self.__dict__.pop("_global_step", None)
+
+
+def _grad_of(p):
+    g = p.grad
+    if g.dtype != torch.bfloat16:
+        raise ValueError("gradients must be bfloat16")
+    return g if g.is_contiguous() else g.contiguous()
+
+
+class _Seeder:
+    """Seeds of one step: deterministic (Triton classes) or from torch's RNG (MuonSR)."""
+
+    def __init__(self, random_seeds: bool):
+        self.random = random_seeds
+
+    def __call__(self, step, idx, salt):
+        if self.random:
+            return int(torch.randint(0, 1 << 32, (1,), dtype=torch.int64).item())
+        return deterministic_seed(step, idx, salt)
+
+
+def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, step, param_idx, seeder):
+    """Per-parameter Muon step (``_triton_muon_step``, triton_muon_sr.py:116-120)."""
+    if p.ndim < 2:
+        raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
+    update = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
+    nsq = torch.zeros(1, dtype=torch.float32, device=p.device) if p.ndim == 2 else None
+    K.muon_prepare([(grad, buf, update, nsq, 0, seeder(step, param_idx, 0))], beta, nesterov)
+    out = K.newton_schulz(update, ns_steps, norm_sq=nsq)
+    K.muon_apply([(p, out, K.ns_scale(p.shape), seeder(step, param_idx, 1))], lr, weight_decay)
+
+
+def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
+                    seeder, owner=None):
+    """Batched step over shape stacks (``_triton_muon_batch_step``, triton_muon_sr.py:128-177).
+
+    Prepare runs once per stack with seed S(step, shape_idx, 0) and counters running over the
+    whole stack; Newton-Schulz runs on chunks of the stack; apply uses
+    S(step, shape_idx * 10000 + i, 1). A stack where only some parameters have gradients
+    falls back to per-parameter steps with param_idx = shape_idx * 10000 + i.
+    ``owner(shape_idx, i) -> bool`` restricts the work to this rank's matrices; seeds and
+    counters stay global, so results do not depend on the number of ranks.
+    """
+    for shape_idx, (shape, grp) in enumerate(shape_groups.items()):
+        active = [p for p in grp if p.grad is not None]
+        if not active:
+            continue
+        stacked_buf = stacked_bufs[shape]
+        if len(active) == len(grp):
+            mine = [i for i in range(len(grp)) if owner is None or owner(shape_idx, i)]
+            if not mine:
+                continue
+            if len(shape) < 2:
+                raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
+            device = stacked_buf.device
+            numel = K.numel_of(shape)
+            work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=device)
+            nsq = torch.zeros(len(mine), dtype=torch.float32, device=device) if len(shape) == 2 else None
+            prep_seed = seeder(step, shape_idx, 0)
+            K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], nsq[j] if nsq is not None else None,
+                             i * numel, prep_seed) for j, i in enumerate(mine)], beta, nesterov)
+            k = max(1, NS_CHUNK_NUMEL // max(1, numel))
+            scale = K.ns_scale(shape)
+            for s in range(0, len(mine), k):
+                out = K.newton_schulz(work[s:s + k], ns_steps, norm_sq=nsq[s:s + k] if nsq is not None else None)
+                K.muon_apply([(grp[mine[s + j]], out[j], scale, seeder(step, shape_idx * 10000 + mine[s + j], 1))
+                              for j in range(out.shape[0])], lr, weight_decay)
+                del out
+            del work
+        else:
+            for p in active:
+                i = buf_indices[id(p)]
+                if owner is not None and not owner(shape_idx, i):
+                    continue
+                muon_single_step(p, _grad_of(p), stacked_buf[i], beta, nesterov, ns_steps, lr, weight_decay,
+                                 step, shape_idx * 10000 + i, seeder)
+
+
+def _check_params(params, name):
+    for p in params:
+        assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+        if p.grad is not None and p.grad.is_sparse:
+            raise RuntimeError(f"{name} does not support sparse gradients")
+
+
+class TritonMuonSR(_StackedBufsMixin, Optimizer):
+    r"""Muon for bf16 matrices with stochastic rounding (drop-in for muon_sr.TritonMuonSR,
+    muon_sr/triton_muon_sr.py:180-255).
+
+    Arguments:
+        params: ndim >= 2 parameters to optimize
+        lr (float): learning rate (default: 0.02)
+        weight_decay (float): weight decay (default: 0)
+        momentum (float): momentum coefficient (default: 0.95)
+        nesterov (bool): Nesterov momentum (default: True)
+        ns_steps (int): Newton-Schulz iterations (default: 5)
+        batch_ns (bool): stacked momentum buffers, Newton-Schulz batched by shape (default: False)
+        shard: optional ``sharding.Sharder`` spreading the matrices over ranks
+    """
+
+    _random_seeds = False
+    _record_step = True
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95, nesterov=True, ns_steps=5, batch_ns=False,
+                 shard=None):
+        defaults = dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
+                        batch_ns=batch_ns)
+        super().__init__(params, defaults)
+        self._batch_state = {}
+        self._shard = shard
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        seeder = _Seeder(self._random_seeds)
+        name = type(self).__name__
+        if self._shard:
+            self._shard.bind(self)
+        for gi, group in enumerate(self.param_groups):
+            lr, wd = group["lr"], group["weight_decay"]
+            beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
+            if group["batch_ns"]:
+                gid = id(group)
+                if gid not in self._batch_state:
+                    self._batch_state[gid] = _init_stacked_bufs(group["params"], group["params"][0].device, self.state)
+                shape_groups, stacked_bufs, buf_indices = self._batch_state[gid]
+                _check_params(group["params"], name)
+                step = 0
+                if self._record_step:
+                    if not hasattr(self, "_global_step"):
+                        self._global_step = _restore_global_step(
+                            self.state, [g for g in self.param_groups if g["batch_ns"]])
+                    self._global_step += 1
+                    step = self._global_step
+                    for p in group["params"]:
+                        self.state[p]["step"] = self._global_step
+                owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
+                muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd, step,
+                                seeder, owner)
+            else:
+                for param_idx, p in enumerate(group["params"]):
+                    assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+                    if p.grad is None:
+                        continue
+                    if p.grad.is_sparse:
+                        raise RuntimeError(f"{name} does not support sparse gradients")
+                    state = self.state[p]
+                    if len(state) == 0:
+                        if self._record_step:
+                            state["step"] = 0
+                        state["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+                    if self._record_step:
+                        state["step"] += 1
+                    if self._shard and not self._shard.owns(gi, param_idx):
+                        continue
+                    muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
+                                     state.get("step", 0), param_idx, seeder)
+        if self._shard:
+            self._shard.sync_params(self)
+        return loss
+
+
+class MuonSR(TritonMuonSR):
+    r"""``muon_sr.MuonSR`` (muon_sr/muon_sr.py:234-302) on the CUDA engine: same arguments and
+    state keys (``momentum_buffer`` only); SR noise seeded from torch's default generator."""
+
+    _random_seeds = True
+    _record_step = False
+
+
+class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
+    r"""Hybrid Muon + AdamW with stochastic rounding (drop-in for
+    muon_sr.TritonMuonSRWithAuxAdam, muon_sr/triton_muon_sr.py:258-373).
+
+    Arguments:
+        param_groups: list of param group dicts, each with a ``use_muon`` flag
+        batch_ns (bool): stacked momentum buffers, Newton-Schulz batched by shape (default: False)
+        shard: optional ``sharding.Sharder`` spreading the work over ranks
+    """
+
+    _random_seeds = False
+    _record_muon_step = True
+
+    def __init__(self, param_groups, batch_ns=False, shard=None):
+        for group in param_groups:
+            assert "use_muon" in group
+            if group["use_muon"]:
+                group.setdefault("lr", 0.02)
+                group.setdefault("momentum", 0.95)
+                group.setdefault("nesterov", True)
+                group.setdefault("ns_steps", 5)
+                group.setdefault("weight_decay", 0)
+            else:
+                group.setdefault("lr", 3e-4)
+                group.setdefault("betas", (0.9, 0.95))
+                group.setdefault("eps", 1e-10)
+                group.setdefault("weight_decay", 0)
+        self.batch_ns = batch_ns
+        self._batch_state = {}
+        self._shard = shard
+        super().__init__(param_groups, {})
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        seeder = _Seeder(self._random_seeds)
+        name = type(self).__name__
+        if self._shard:
+            self._shard.bind(self)
+        param_offset = 0
+        for gi, group in enumerate(self.param_groups):
+            group_offset = param_offset
+            param_offset += len(group["params"])
+            if group["use_muon"]:
+                lr, wd = group["lr"], group["weight_decay"]
+                beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
+                if not group["params"]:
+                    continue
+                if self.batch_ns:
+                    gid = id(group)
+                    if gid not in self._batch_state:
+                        self._batch_state[gid] = _init_stacked_bufs(group["params"], group["params"][0].device,
+                                                                     self.state)
+                    shape_groups, stacked_bufs, buf_indices = self._batch_state[gid]
+                    _check_params(group["params"], name)
+                    step = 0
+                    if self._record_muon_step:
+                        if not hasattr(self, "_global_step"):
+                            self._global_step = _restore_global_step(
+                                self.state, [g for g in self.param_groups if g["use_muon"]])
+                        self._global_step += 1
+                        step = self._global_step
+                        for p in group["params"]:
+                            self.state[p]["step"] = self._global_step
+                    owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
+                    muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd,
+                                    step, seeder, owner)
+                else:
+                    for param_idx, p in enumerate(group["params"]):
+                        assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+                        if p.grad is None:
+                            continue
+                        if p.grad.is_sparse:
+                            raise RuntimeError(f"{name} does not support sparse gradients")
+                        state = self.state[p]
+                        if len(state) == 0:
+                            if self._record_muon_step:
+                                state["step"] = 0
+                            state["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+                        if self._record_muon_step:
+                            state["step"] += 1
+                        if self._shard and not self._shard.owns(gi, param_idx):
+                            continue
+                        muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
+                                         state.get("step", 0), param_idx, seeder)
+            else:
+                lr = group["lr"]
+                beta1, beta2 = group["betas"]
+                eps, wd = group["eps"], group["weight_decay"]
+                items = []
+                for i, p in enumerate(group["params"]):
+                    assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+                    if p.grad is None:
+                        continue
+                    if p.grad.is_sparse:
+                        raise RuntimeError(f"{name} does not support sparse gradients")
+                    state = self.state[p]
+                    if len(state) == 0:
+                        state["step"] = 0
+                        state["ema"] = torch.zeros_like(p, dtype=torch.bfloat16)
+                        state["ema_squared"] = torch.zeros_like(p, dtype=torch.bfloat16)
+                    state["step"] += 1
+                    if self._shard and not self._shard.owns(gi, i):
+                        continue
+                    items.append((p, _grad_of(p), state["ema"], state["ema_squared"], state["step"],
+                                  seeder(state["step"], group_offset + i, 0)))
+                K.adamw_sr(items, lr, beta1, beta2, eps, wd)
+        if self._shard:
+            self._shard.sync_params(self)
+        return loss
+
+
+class MuonSRWithAuxAdam(TritonMuonSRWithAuxAdam):
+    r"""``muon_sr.MuonSRWithAuxAdam`` (muon_sr/muon_sr.py:305-418) on the CUDA engine: same
+    arguments and state keys; SR noise seeded from torch's default generator."""
+
+    _random_seeds = True
+    _record_muon_step = False

@@ -1,0 +1,113 @@
+"""Parameter-sharded optimizer work across the ranks of one node.
+
+The reference is single-device; data-parallel replicas each run the whole optimizer step
+and stay identical because the rounding seeds depend only on (step, index). Here each rank
+runs the step for the parameters it owns and the updated bf16 weights are then shared over
+NCCL (NVLink / NVSwitch), so the step's work is divided by the number of ranks.
+
+* Partition: whole tensors (Newton-Schulz needs each full matrix), longest-processing-time
+  greedy on an estimated B200 time per tensor -- Newton-Schulz FLOPs at the tensor-core rate
+  for Muon matrices, bytes at the HBM rate for AdamW / 8-bit tensors.
+* Seeds and Philox counters stay global, so every rank writes exactly the bits a single GPU
+  would (Newton-Schulz computes each matrix independently of how the batch is chunked).
+* Sharing: after the step every updated parameter is broadcast from its owner; the NCCL
+  calls are enqueued after the kernels on the current stream and overlap nothing else in
+  this version.
+* Optimizer state (momentum, moments) stays with the owner; ``state_dict()`` on a rank holds
+  valid values only for the parameters that rank owns.
+"""
+import heapq
+
+import torch
+import torch.distributed as dist
+
+TENSOR_FLOPS = 1.4e15   # sustained dense bf16 on B200, used only to weigh the partition
+HBM_BYTES = 6.5e12
+
+
+def _ns_flops(shape, steps=5):
+    r, c = shape[-2], shape[-1]
+    m, n = min(r, c), max(r, c)
+    batch = 1
+    for s in shape[:-2]:
+        batch *= s
+    return batch * steps * (4 * m * m * n + 2 * m ** 3)
+
+
+def _cost(p, use_muon, ns_steps):
+    numel = p.numel()
+    if use_muon and p.ndim >= 2:
+        return _ns_flops(tuple(p.shape), ns_steps) / TENSOR_FLOPS + 14 * numel / HBM_BYTES
+    return 14 * numel / HBM_BYTES
+
+
+class Sharder:
+    """Spreads the per-parameter optimizer work of one optimizer over a process group."""
+
+    def __init__(self, group=None):
+        if not dist.is_available() or not dist.is_initialized():
+            raise RuntimeError("Sharder needs an initialised torch.distributed process group")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._owner = None  # id(param) -> rank within the group
+        self._order = None  # params in a fixed order for the broadcasts
+
+    # -- plan -----------------------------------------------------------------------------
+    def plan(self, param_groups):
+        """Assign every parameter to a rank (same result on every rank)."""
+        entries = []
+        for gi, g in enumerate(param_groups):
+            use_muon = g.get("use_muon", "momentum" in g and "betas" not in g)
+            for pi, p in enumerate(g["params"]):
+                entries.append((_cost(p, use_muon, g.get("ns_steps", 5)), gi, pi, p))
+        # Largest first; ties broken by position so that the plan is deterministic.
+        entries.sort(key=lambda e: (-e[0], e[1], e[2]))
+        heap = [(0.0, r) for r in range(self.world)]
+        owner = {}
+        for cost, gi, pi, p in entries:
+            load, r = heapq.heappop(heap)
+            owner[id(p)] = r
+            heapq.heappush(heap, (load + cost, r))
+        self._owner = owner
+        self._order = [p for g in param_groups for p in g["params"]]
+        return owner
+
+    def loads(self, param_groups):
+        """Estimated seconds of work per rank under the current plan."""
+        out = [0.0] * self.world
+        for g in param_groups:
+            use_muon = g.get("use_muon", "momentum" in g and "betas" not in g)
+            for p in g["params"]:
+                out[self._owner[id(p)]] += _cost(p, use_muon, g.get("ns_steps", 5))
+        return out
+
+    def _ensure(self, optimizer):
+        if self._owner is None or any(id(p) not in self._owner for g in optimizer.param_groups for p in g["params"]):
+            self.plan(optimizer.param_groups)
+
+    # -- queries used by the optimizers -----------------------------------------------------
+    def bind(self, optimizer):
+        self._ensure(optimizer)
+        self._groups = optimizer.param_groups
+        return self
+
+    def owns(self, gi, pi) -> bool:
+        return self._owner[id(self._groups[gi]["params"][pi])] == self.rank
+
+    def muon_owner(self, gi, shape_groups):
+        stacks = list(shape_groups.values())
+        return lambda shape_idx, i: self._owner[id(stacks[shape_idx][i])] == self.rank
+
+    # -- weight sharing ----------------------------------------------------------------------
+    def sync_params(self, optimizer):
+        """Broadcast every parameter that has a gradient from its owner to all ranks."""
+        works = []
+        for p in self._order:
+            if p.grad is None:
+                continue
+            src = self._owner[id(p)]
+            src_global = dist.get_global_rank(self.group, src) if self.group is not None else src
+            works.append(dist.broadcast(p.data, src=src_global, group=self.group, async_op=True))
+        for w in works:
+            w.wait()

@@ -1,0 +1,54 @@
+"""The C-ABI library loads and exports every entry point the public header declares
+(CPU only: nothing here launches a kernel)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from muon_sr_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "muon_sr_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(msr_\w+)\s*\(", text)))
+
+
+def test_library_exists_and_loads():
+    assert os.path.exists(_lib.LIB_PATH), "build the library first: python -m muon_sr_b200.build"
+    lib = _lib.load()
+    assert lib.msr_abi_version() == 1
+
+
+def test_every_declared_symbol_is_exported():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    names = declared_functions()
+    assert len(names) >= 12
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    bound = {name for name, _, _ in _lib.SIGNATURES}
+    assert bound == set(declared_functions())
+
+
+def test_status_strings_and_argument_errors_without_gpu():
+    lib = _lib.load()
+    assert lib.msr_status_string(0) == b"ok"
+    assert lib.msr_status_string(4) == b"workspace too small"
+    # argument validation happens before any CUDA call
+    assert lib.msr_grad_accum_bf16(None, None, -1, 0, 0, None) == 1
+    assert b"negative" in lib.msr_last_error()
+    assert lib.msr_newton_schulz_bf16(None, None, 1, 8, 8, 5, None, None, 0, None) == 1
+    assert lib.msr_ns_workspace_bytes(0, 8, 8) == 0
+
+
+def test_ns_workspace_accounts_for_padding():
+    lib = _lib.load()
+    plain = lib.msr_ns_workspace_bytes(4, 64, 128)
+    padded = lib.msr_ns_workspace_bytes(4, 63, 127)
+    assert plain > 0 and padded > plain  # padded shapes need two more staging buffers

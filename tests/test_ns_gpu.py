@@ -1,0 +1,112 @@
+"""The tcgen05 GEMM and the Newton-Schulz chain on the GPU.
+
+* GEMM: every operand majorness combination against a torch fp32 reference of the same
+  product, with the fused epilogue (alpha, beta * C, per-matrix scale powers), on tile-
+  aligned and ragged shapes. Tolerance: bf16 output rounding (rel. Frobenius <= 1e-2,
+  typically ~2e-3).
+* Newton-Schulz: against the reference's own ``_newton_schulz`` outputs (golden, CPU) and
+  against the same torch ops run on this GPU, north-star tolerance rel. Frobenius <= 1e-2.
+"""
+import numpy as np
+import pytest
+import torch
+
+from muon_sr_b200 import kernels as K
+from oracle.newton_schulz import newton_schulz as ns_ref
+from oracle.newton_schulz import rel_frobenius
+from tests._golden import load, to_bf16
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+NS_TOL = 1e-2
+
+
+def _ref_gemm(a, a_mn, b, b_mn, c, alpha, beta, scale, ap, bp):
+    A = a.float().transpose(1, 2) if a_mn else a.float()      # [batch, M, K]
+    B = b.float() if b_mn else b.float().transpose(1, 2)      # [batch, K, N]
+    acc = A @ B
+    al = torch.full((a.shape[0], 1, 1), alpha, device=a.device)
+    be = torch.full((a.shape[0], 1, 1), beta, device=a.device)
+    if scale is not None:
+        s = scale.view(-1, 1, 1)
+        al = al * s ** ap
+        be = be * s ** bp
+    out = al * acc
+    if c is not None:
+        out = out + be * c.float()
+    return out
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("shape", [(2, 128, 256, 64), (3, 256, 512, 320), (2, 200, 264, 136), (1, 8, 16, 24),
+                                   (2, 384, 768, 1024)])
+def test_gemm_vs_torch(a_mn, b_mn, shape):
+    batch, M, N, Kd = shape
+    g = torch.Generator(device=DEV).manual_seed(sum(shape) + 10 * a_mn + b_mn)
+    a = torch.randn(batch, *((Kd, M) if a_mn else (M, Kd)), device=DEV, generator=g).bfloat16()
+    b = torch.randn(batch, *((Kd, N) if b_mn else (N, Kd)), device=DEV, generator=g).bfloat16()
+    c = torch.randn(batch, M, N, device=DEV, generator=g).bfloat16()
+    scale = torch.rand(batch, device=DEV, generator=g) + 0.5
+    for alpha, beta, cc, sc, ap, bp in ((1.0, 0.0, None, None, 0, 0), (2.0315, -4.775, c, None, 0, 0),
+                                         (1.0, 3.4445, c, scale, 1, 1), (1.0, 0.0, None, scale, 2, 0)):
+        d = K.gemm_bf16(a, a_mn, b, b_mn, cc, alpha, beta, sc, ap, bp)
+        ref = _ref_gemm(a, a_mn, b, b_mn, cc, alpha, beta, sc, ap, bp)
+        err = rel_frobenius(d, ref)
+        assert err < 1e-2, (shape, a_mn, b_mn, alpha, beta, err)
+    assert K.device_error() == 0
+
+
+def test_ns_matches_reference_golden():
+    d = load("newton_schulz.npz")
+    for k in range(int(d["count"])):
+        shp = tuple(d[f"shape{k}"].tolist())
+        x = to_bf16(d[f"x{k}"], DEV).view(*shp)
+        y = K.newton_schulz(x, 5)
+        ref = to_bf16(d[f"y{k}"], DEV).view(*shp)
+        err = rel_frobenius(y, ref)
+        assert err < NS_TOL, (shp, err)
+
+
+@pytest.mark.parametrize("shape", [(4, 256, 512), (4, 512, 256), (2, 768, 768), (2, 768, 3072), (2, 3072, 768),
+                                   (3, 100, 300), (2, 333, 77), (1, 1024, 4096)])
+def test_ns_matches_torch_on_gpu(shape):
+    g = torch.Generator(device=DEV).manual_seed(shape[1] * 7 + shape[2])
+    x = (torch.randn(*shape, device=DEV, generator=g) * 1e-3).bfloat16()
+    y = K.newton_schulz(x, 5)
+    ref = ns_ref(x, 5, None)
+    err = rel_frobenius(y, ref)
+    assert err < NS_TOL, (shape, err)
+    assert torch.isfinite(y.float()).all()
+
+
+def test_ns_given_norm_equals_computed_norm():
+    x = (torch.randn(3, 256, 384, device=DEV) * 1e-2).bfloat16()
+    nsq = (x.float() ** 2).sum(dim=(1, 2)).contiguous()
+    a = K.newton_schulz(x, 5)
+    b = K.newton_schulz(x, 5, norm_sq=nsq)
+    assert rel_frobenius(a, b) < 1e-3
+
+
+def test_ns_is_independent_of_batching():
+    """Each matrix is computed on its own: batch composition never changes its bits."""
+    x = (torch.randn(6, 256, 512, device=DEV) * 1e-3).bfloat16()
+    whole = K.newton_schulz(x, 5)
+    parts = torch.cat([K.newton_schulz(x[i:i + 2].contiguous(), 5) for i in range(0, 6, 2)])
+    assert torch.equal(whole.view(torch.int16), parts.view(torch.int16))
+
+
+def test_ns_steps_zero_and_one():
+    x = (torch.randn(2, 64, 96, device=DEV) * 1e-3).bfloat16()
+    for steps in (0, 1, 2):
+        y = K.newton_schulz(x, steps)
+        assert rel_frobenius(y, ns_ref(x, steps, None)) < NS_TOL
+
+
+def test_ns_orthogonality_llama_shape():
+    """Size-independent property at a full config shape: singular values of NS(X) land in
+    the quintic's band (the coefficients do not converge to exactly 1)."""
+    x = (torch.randn(1, 4096, 14336, device=DEV) * 1e-3).bfloat16()
+    y = K.newton_schulz(x, 5)
+    s = torch.linalg.svdvals(y[0].float())
+    assert float(s.max()) < 1.3 and float(s.min()) > 0.5, (float(s.min()), float(s.max()))
+    assert K.device_error() == 0

@@ -1,0 +1,202 @@
+"""Whole optimizer steps through the public API on the GPU, against trajectories the
+reference's own classes produced (golden, CPU): momentum and AdamW tensors bit-exact;
+Muon weights within 1-2 bf16 ulps (they sit downstream of Newton-Schulz, whose bf16
+GEMMs differ between the reference's CPU run and the tensor cores within 1e-2)."""
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from muon_sr_b200 import (TritonAdamW, TritonAdamW8bit, TritonMuonSR, TritonMuonSRWithAuxAdam,
+                          TritonSRAccumulator, MuonSR, MuonSRWithAuxAdam, SRAccumulator)
+from muon_sr_b200 import kernels as K
+from oracle import adamw8bit as o8
+from oracle.sr import bf16_to_f32
+from tests._golden import assert_bits_equal, bits_of, load, to_bf16
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+MUON_SHAPES = [(24, 40), (24, 40), (40, 24), (24, 40), (40, 24), (16, 16)]
+ADAM_SHAPES = [(30, 16), (16,), (16,)]
+
+
+def _ulp_diff(a_bits, b_bits):
+    a = bf16_to_f32(a_bits).astype(np.float64)
+    b = bf16_to_f32(b_bits).astype(np.float64)
+    ulp = np.abs(bf16_to_f32((b_bits.astype(np.uint32) + 1).astype(np.uint16)) - b) + 1e-30
+    return np.abs(a - b) / ulp
+
+
+@pytest.mark.parametrize("batch_ns,fname", [(True, "traj_hybrid_batch.npz"), (False, "traj_hybrid_nobatch.npz")])
+def test_hybrid_trajectory(batch_ns, fname):
+    d = load(fname)
+    shapes = MUON_SHAPES + ADAM_SHAPES
+    params = [torch.nn.Parameter(to_bf16(d[f"init_{i}"], DEV).view(*s)) for i, s in enumerate(shapes)]
+    mp, ap = params[:6], params[6:]
+    opt = TritonMuonSRWithAuxAdam([
+        dict(params=mp, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+        dict(params=ap, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
+    ], batch_ns=batch_ns)
+    for step in range(4):
+        for i, p in enumerate(params):
+            g = d[f"g{step}_{i}"]
+            p.grad = None if g.size == 0 else to_bf16(g, DEV).view(p.shape)
+        opt.step()
+        for i, p in enumerate(params):
+            st = opt.state[p]
+            assert int(st.get("step", -1)) == int(d[f"step{step}_{i}"]), ("step", step, i)
+            for key in ("momentum_buffer", "ema", "ema_squared"):
+                k = f"{key}{step}_{i}"
+                if k in d:
+                    assert_bits_equal(bits_of(st[key]).ravel(), d[k].ravel(), f"{key} step {step} param {i}")
+            want = d[f"p{step}_{i}"].ravel()
+            got = bits_of(p).ravel()
+            if i >= 6:
+                assert_bits_equal(got, want, f"AdamW param {i} step {step}")
+            else:
+                ud = _ulp_diff(got, want)
+                assert ud.max() <= 2.0 + 1e-9, (step, i, ud.max())
+                assert (ud > 0).mean() < 0.05, (step, i, (ud > 0).mean())
+
+
+def test_adamw_centralization_trajectory():
+    d = load("traj_adamw_central.npz")
+    shapes = [(12, 20), (20,)]
+    params = [torch.nn.Parameter(to_bf16(d[f"init_{i}"], DEV).view(*s)) for i, s in enumerate(shapes)]
+    opt = TritonAdamW(params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, centralization=0.5)
+    for step in range(3):
+        for i, p in enumerate(params):
+            p.grad = to_bf16(d[f"g{step}_{i}"], DEV).view(p.shape)
+        opt.step()
+        for i, p in enumerate(params):
+            # the centralised gradient's fp32 mean may differ in its last bit between CPU
+            # and GPU reductions, so allow 1 ulp on a small fraction of elements
+            for got, want in ((bits_of(p), d[f"p{step}_{i}"]), (bits_of(opt.state[p]["ema"]), d[f"ema{step}_{i}"])):
+                ud = _ulp_diff(got.ravel(), want.ravel())
+                assert ud.max() <= 1.0 + 1e-9 and (ud > 0).mean() < 0.05, (step, i, ud.max())
+
+
+def test_sr_accumulator_trajectory():
+    d = load("traj_accum.npz")
+    model = torch.nn.Sequential(torch.nn.Linear(16, 24), torch.nn.Linear(24, 8)).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        for i, p in enumerate(model.parameters()):
+            p.copy_(to_bf16(d[f"init_{i}"], DEV).view(p.shape))
+    TritonSRAccumulator.assign_hooks(model)
+    random.seed(0)
+    xb = to_bf16(d["x"], DEV).view(4, 5, 16)
+    for k in range(4):
+        model(xb[k]).float().pow(2).mean().backward()
+    for i, p in enumerate(model.parameters()):
+        # autograd on the GPU and on the CPU can differ in a gradient's last bit; compare
+        # with a 1-ulp allowance on the accumulated sum
+        ud = _ulp_diff(bits_of(p.acc_grad).ravel(), d[f"acc_{i}"].ravel())
+        assert ud.max() <= 2.0 + 1e-9, (i, ud.max())
+    TritonSRAccumulator.reassign_grad_buffer(model)
+    for i, p in enumerate(model.parameters()):
+        assert p.grad is not None and not hasattr(p, "acc_grad")
+
+
+def test_adamw8bit_optimizer_vs_oracle_and_checkpoint():
+    torch.manual_seed(0)
+    shapes = [(64, 96), (100,), (4096,), (33, 128)]
+    params = [torch.nn.Parameter((torch.randn(*s) * 0.02).bfloat16().to(DEV)) for s in shapes]
+    opt = TritonAdamW8bit([dict(params=params[:3]), dict(params=params[3:], optim_bits=16)], lr=1e-3,
+                          weight_decay=0.01, block_size=128)
+    Q1, Q2 = o8.create_dynamic_map(True), o8.create_dynamic_map(False)
+    ref = {}
+    for i, p in enumerate(params):
+        n = p.numel()
+        quant = n >= 4096 and i < 3
+        ref[i] = dict(p=bits_of(p).ravel(), quant=quant,
+                      s1=np.full(n, 127, np.uint8) if quant else np.zeros(n, np.uint16),
+                      s2=np.zeros(n, np.uint8) if quant else np.zeros(n, np.uint16),
+                      a1=np.zeros((n + 127) // 128, np.float32) if quant else None,
+                      a2=np.zeros((n + 127) // 128, np.float32) if quant else None)
+    for step in (1, 2, 3):
+        for i, p in enumerate(params):
+            p.grad = (torch.randn(p.shape) * 1e-3).bfloat16().to(DEV)
+            r = ref[i]
+            seed = (step * 2654435761 ^ i * 1234567891) & 0xFFFFFFFF
+            r["p"], r["s1"], r["s2"], r["a1"], r["a2"] = o8.adamw8bit(
+                r["p"], bits_of(p.grad).ravel(), r["s1"], r["s2"], r["a1"], r["a2"], Q1, Q2, 1e-3, 0.9, 0.999,
+                1e-8, 0.01, step, seed, 128, r["quant"])
+        opt.step()
+        for i, p in enumerate(params):
+            st = opt.state[p]
+            assert st["step"] == step and st["format_version"] == 2 and st["optim_bits"] == (8 if ref[i]["quant"] else 16)
+            assert_bits_equal(bits_of(p).ravel(), ref[i]["p"], f"p {i} step {step}")
+            if ref[i]["quant"]:
+                assert_bits_equal(st["state1"].cpu().numpy().ravel(), ref[i]["s1"], "codes1")
+                assert_bits_equal(st["absmax2"].cpu().numpy().view(np.uint32), ref[i]["a2"].view(np.uint32), "a2")
+            else:
+                assert_bits_equal(bits_of(st["state1"]).ravel(), ref[i]["s1"], "bf16 m")
+    sd = opt.state_dict()
+    opt2 = TritonAdamW8bit([dict(params=params[:3]), dict(params=params[3:], optim_bits=16)], lr=1e-3,
+                           weight_decay=0.01, block_size=128)
+    opt2.load_state_dict(sd)
+    for i, p in enumerate(params):
+        a, b = opt.state[p], opt2.state[p]
+        assert a["state1"].dtype == b["state1"].dtype and torch.equal(a["state1"], b["state1"])
+    bad = TritonAdamW8bit([dict(params=params[:3]), dict(params=params[3:], optim_bits=16)], block_size=64)
+    with pytest.raises(ValueError):
+        bad.load_state_dict(sd)
+
+
+def test_batch_ns_state_dict_roundtrip_continues_identically():
+    torch.manual_seed(1)
+    shapes = [(64, 128)] * 3 + [(128, 64)] * 2
+    def make():
+        return [torch.nn.Parameter((torch.randn(*s, generator=torch.Generator().manual_seed(i)) * 0.02)
+                                   .bfloat16().to(DEV)) for i, s in enumerate(shapes)]
+    grads = [[(torch.randn(*s) * 1e-3).bfloat16().to(DEV) for s in shapes] for _ in range(4)]
+    pa, pb = make(), make()
+    oa = TritonMuonSR(pa, batch_ns=True, weight_decay=0.01)
+    for k in range(2):
+        for p, g in zip(pa, grads[k]):
+            p.grad = g
+        oa.step()
+    ob = TritonMuonSR(pb, batch_ns=True, weight_decay=0.01)
+    with torch.no_grad():
+        for x, y in zip(pa, pb):
+            y.copy_(x)
+    ob.load_state_dict(oa.state_dict())
+    for k in range(2, 4):
+        for p, q, g in zip(pa, pb, grads[k]):
+            p.grad = g
+            q.grad = g.clone()
+        oa.step()
+        ob.step()
+    for x, y in zip(pa, pb):
+        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+
+
+def test_pure_torch_named_variants_run():
+    """MuonSR / MuonSRWithAuxAdam / SRAccumulator keep the reference's names and state keys."""
+    p = torch.nn.Parameter((torch.randn(32, 48) * 0.02).bfloat16().to(DEV))
+    q = torch.nn.Parameter((torch.randn(48) * 0.02).bfloat16().to(DEV))
+    opt = MuonSRWithAuxAdam([dict(params=[p], use_muon=True), dict(params=[q], use_muon=False)], batch_ns=True)
+    p.grad = (torch.randn_like(p) * 1e-3)
+    q.grad = (torch.randn_like(q) * 1e-3)
+    opt.step()
+    assert set(opt.state[p].keys()) == {"momentum_buffer"}
+    assert set(opt.state[q].keys()) == {"step", "ema", "ema_squared"}
+    o2 = MuonSR([p])
+    p.grad = (torch.randn_like(p) * 1e-3)
+    o2.step()
+    assert set(o2.state[p].keys()) == {"momentum_buffer"}
+    m = torch.nn.Linear(8, 8).to(DEV, torch.bfloat16)
+    SRAccumulator.assign_hooks(m)
+    for _ in range(2):
+        m(torch.randn(2, 8, device=DEV, dtype=torch.bfloat16)).sum().backward()
+    SRAccumulator.reassign_grad_buffer(m)
+    assert m.weight.grad is not None
+
+
+def test_library_failures_raise():
+    x = torch.zeros(4, 8, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="alias"):
+        K.newton_schulz(x, 5, out=x)
+    with pytest.raises(ValueError):
+        K.newton_schulz(x.float(), 5)
