@@ -157,27 +157,38 @@ int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, const float* qm
 /* ---- Newton-Schulz ---------------------------------------------------------------------
  * out[b] = NS_steps(x[b]) for b < batch, x and out bf16 [batch, rows, cols] contiguous.
  * Quintic iteration (a, b, c) = (3.4445, -4.7750, 2.0315) on the wide orientation
- * (X^T when rows > cols), normalised by 1/(||x[b]||_F + 1e-7). Each step is three
- * batched tcgen05 GEMMs with fused epilogues: A = X X^T, B = c*(A A) + b*A,
- * X' = B X + a*X. norm_sq, if given, holds ||x[b]||_F^2 (e.g. from msr_muon_prepare);
- * otherwise it is computed. out must not alias x.
+ * (X^T when rows > cols), normalised by the Frobenius norm. Each step is three batched
+ * tcgen05 GEMMs with fused epilogues: A = X X^T, B = c*(A A) + b*A, X' = B X + a*X.
+ * mode MSR_NS_REFERENCE_ROUNDING rounds to bf16 exactly where the reference's torch ops
+ * do -- X0 = bf16(x / bf16(bf16(||x||) + 1e-7)), A = bf16(acc),
+ * B = bf16(bf16(b*A) + bf16(c*bf16(acc))), X' = bf16(bf16(a*X) + bf16(acc)) -- with
+ * every rounding inside the GEMM epilogues. mode MSR_NS_FUSED_ROUNDING rounds once per
+ * GEMM (alpha*acc + beta*C in fp32) and folds 1/(||x||+1e-7) into the first step; it is
+ * closer to exact arithmetic but further from the reference's bits.
+ * norm_sq, if given, holds ||x[b]||_F^2 (e.g. from msr_muon_prepare); otherwise it is
+ * computed. out must not alias x.
  * Replaces _newton_schulz (muon_sr/muon_sr.py:82-98) with out_dtype=None, as called at
  * muon_sr/triton_muon_sr.py:119 and :166. */
+enum msr_ns_mode { MSR_NS_REFERENCE_ROUNDING = 0, MSR_NS_FUSED_ROUNDING = 1 };
+
 size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
 
 int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
-                           int steps, const float* norm_sq, void* workspace, size_t workspace_bytes,
-                           msr_stream_t stream);
+                           int steps, int mode, const float* norm_sq, void* workspace,
+                           size_t workspace_bytes, msr_stream_t stream);
 
 /* ---- batched bf16 GEMM with the Newton-Schulz epilogue (test hook) --------------------
  * d[b] = alpha_b * (A[b] x B[b]^T) + beta_b * c[b] on the tensor cores, bf16 in/out,
  * fp32 accumulate. A is [batch, M, K] (a_mn_major = 0) or [batch, K, M] (1); B is
  * [batch, N, K] (b_mn_major = 0) or [batch, K, N] (1); c, d are [batch, M, N]; c may be
  * NULL. alpha_b = alpha * s^alpha_pow, beta_b = beta * s^beta_pow with s = scale[b]
- * (scale may be NULL). Rows of every operand must be a multiple of 16 bytes. */
+ * (scale may be NULL). With ref_rounding != 0 the epilogue instead computes
+ * bf16(bf16(beta*c) + bf16(alpha*bf16(acc))) (the reference's op-by-op rounding; no scale).
+ * Rows of every operand must be a multiple of 16 bytes. */
 int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c,
                   void* d, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha, float beta,
-                  const float* scale, int alpha_pow, int beta_pow, msr_stream_t stream);
+                  const float* scale, int alpha_pow, int beta_pow, int ref_rounding,
+                  msr_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -67,10 +67,10 @@ SIGNATURES = [
     ("msr_adamw8bit", c_int, [ctypes.POINTER(Adam8Entry), c_int, c_void_p, c_void_p,
                               ctypes.POINTER(Adam8Hparams), c_void_p]),
     ("msr_ns_workspace_bytes", c_size_t, [c_int64, c_int64, c_int64]),
-    ("msr_newton_schulz_bf16", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p,
+    ("msr_newton_schulz_bf16", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p,
                                        c_void_p, c_size_t, c_void_p]),
     ("msr_gemm_bf16", c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
-                              c_int64, c_float, c_float, c_void_p, c_int, c_int, c_void_p]),
+                              c_int64, c_float, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
 ]
 
 _lib = None

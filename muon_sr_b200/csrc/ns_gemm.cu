@@ -61,7 +61,10 @@ struct Params {
   float alpha, beta;
   const float* scale;      // per matrix; interpreted as ||x||_F^2 when scale_is_norm_sq
   int alpha_pow, beta_pow, scale_is_norm_sq;
+  int ref_round;           // 1: bf16(bf16(beta*C) + bf16(alpha*bf16(acc))), the torch-op rounding
 };
+
+__device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(rne_bf16_bits(x)); }
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
 
@@ -260,10 +263,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int j = 0; j < 8; ++j) cin[j] = 0.f;
               }
               U16x8 o;
+              if (p.ref_round) {
+                const bool has_c = crow != nullptr && beta != 0.f;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float accv = __uint_as_float(v[g * 8 + j]);
-                o.v[j] = rne_bf16_bits(fmaf(alpha, accv, beta * cin[j]));
+                for (int j = 0; j < 8; ++j) {
+                  const float t = bf16r(__fmul_rn(alpha, bf16r(__uint_as_float(v[g * 8 + j]))));
+                  o.v[j] = has_c ? rne_bf16_bits(__fadd_rn(bf16r(__fmul_rn(beta, cin[j])), t)) : rne_bf16_bits(t);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float accv = __uint_as_float(v[g * 8 + j]);
+                  o.v[j] = rne_bf16_bits(fmaf(alpha, accv, beta * cin[j]));
+                }
               }
               if (full) {
                 st_u16x8(drow + col, o);
@@ -350,7 +362,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
 int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn, int64_t b_bstride, const void* c,
          int64_t ldc, int64_t c_bstride, void* d, int64_t ldd, int64_t d_bstride, int64_t batch, int64_t M, int64_t N,
          int64_t K, float alpha, float beta, const float* scale, int alpha_pow, int beta_pow, int scale_is_norm_sq,
-         cudaStream_t s) {
+         int ref_round, cudaStream_t s) {
   CUtensorMap ta, tb;
   int st = a_mn ? make_map(&ta, a, M, K, batch, a_bstride, 64) : make_map(&ta, a, K, M, batch, a_bstride, BM);
   if (st) return st;
@@ -366,6 +378,7 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
   p.ldd = ldd; p.ldc = ldc; p.d_bstride = d_bstride; p.c_bstride = c_bstride;
   p.alpha = alpha; p.beta = beta;
   p.scale = scale; p.alpha_pow = alpha_pow; p.beta_pow = beta_pow; p.scale_is_norm_sq = scale_is_norm_sq;
+  p.ref_round = ref_round;
   if (a_mn && b_mn) return launch<1, 1>(ta, tb, p, s);
   if (a_mn) return launch<1, 0>(ta, tb, p, s);
   if (b_mn) return launch<0, 1>(ta, tb, p, s);
@@ -408,17 +421,28 @@ __global__ void pad_copy_kernel(const uint16_t* __restrict__ src, int64_t sR, in
   }
 }
 
-// out = RNE(x * 1/(||x||+1e-7)): Newton-Schulz with zero steps.
-__global__ void scale_copy_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ out, int64_t per,
-                                  int64_t batch, const float* __restrict__ nsq) {
+// Normalisation by the Frobenius norm (may run in place).
+//  ref != 0: out = bf16(x / d), d = bf16(bf16(sqrt(norm_sq)) + 1e-7): the reference's bf16 ops
+//            X / (X.norm() + 1e-7) on a bf16 tensor (muon_sr/muon_sr.py:91).
+//  ref == 0: out = bf16(x * (1 / (sqrt(norm_sq) + 1e-7))) in fp32.
+__global__ void normalize_kernel(const uint16_t* x, uint16_t* out, int64_t per, int64_t batch,
+                                 const float* __restrict__ nsq, int ref) {
   const int64_t total = per * batch;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const float s = 1.0f / (sqrtf(nsq[i / per]) + 1e-7f);
-    out[i] = rne_bf16_bits(bf16_bits_to_f32(x[i]) * s);
+    const float nrm = sqrtf(nsq[i / per]);
+    const float v = bf16_bits_to_f32(x[i]);
+    if (ref) {
+      const float d = bf16r(__fadd_rn(bf16r(nrm), 1e-7f));
+      out[i] = rne_bf16_bits(__fdiv_rn(v, d));
+    } else {
+      out[i] = rne_bf16_bits(v * (1.0f / (nrm + 1e-7f)));
+    }
   }
 }
 
 inline int64_t round8(int64_t v) { return (v + 7) / 8 * 8; }
+struct NsLayout;
+int64_t xs_elems(const NsLayout& L);
 inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 struct NsLayout {
@@ -448,6 +472,8 @@ NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
   return L;
 }
 
+int64_t xs_elems(const NsLayout& L) { return L.R8 * L.C8; }
+
 }  // namespace gemm
 }  // namespace msr
 
@@ -471,7 +497,7 @@ int msr_device_error(msr_stream_t stream, int clear) {
 
 int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c, void* d, int64_t batch,
                   int64_t M, int64_t N, int64_t K, float alpha, float beta, const float* scale, int alpha_pow,
-                  int beta_pow, msr_stream_t stream) {
+                  int beta_pow, int ref_rounding, msr_stream_t stream) {
   if (!a || !b || !d || batch <= 0 || M <= 0 || N <= 0 || K <= 0)
     return fail(MSR_ERR_INVALID, "msr_gemm_bf16: null pointer or non-positive size");
   const int64_t a_inner = a_mn_major ? M : K, b_inner = b_mn_major ? N : K;
@@ -479,8 +505,8 @@ int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, 
     return fail(MSR_ERR_INVALID, "msr_gemm_bf16: contiguous dims must be multiples of 8 (got A %lld, B %lld, N %lld)",
                 (long long)a_inner, (long long)b_inner, (long long)N);
   if (int st = require_sm100()) return st;
-  return run_gemm(a, a_mn_major, M * K, b, b_mn_major, N * K, c, N, M * N, d, N, M * N, batch, M, N, K, alpha, beta, scale,
-              alpha_pow, beta_pow, 0, to_stream(stream));
+  return run_gemm(a, a_mn_major, M * K, b, b_mn_major, N * K, c, N, M * N, d, N, M * N, batch, M, N, K, alpha, beta,
+                  ref_rounding ? nullptr : scale, alpha_pow, beta_pow, 0, ref_rounding ? 1 : 0, to_stream(stream));
 }
 
 size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols) {
@@ -488,10 +514,13 @@ size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols) {
   return ns_layout(batch, rows, cols).total;
 }
 
-int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols, int steps,
+int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols, int steps, int mode,
                            const float* norm_sq, void* workspace, size_t workspace_bytes, msr_stream_t stream) {
   if (!x || !out || batch <= 0 || rows <= 0 || cols <= 0 || steps < 0)
     return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: null pointer or bad size");
+  if (mode != MSR_NS_REFERENCE_ROUNDING && mode != MSR_NS_FUSED_ROUNDING)
+    return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: unknown mode %d", mode);
+  const int ref = mode == MSR_NS_REFERENCE_ROUNDING;
   if (x == out) return fail(MSR_ERR_INVALID, "msr_newton_schulz_bf16: out must not alias x");
   const NsLayout L = ns_layout(batch, rows, cols);
   if (workspace == nullptr || workspace_bytes < L.total)
@@ -515,8 +544,9 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
   }
   const int ew_grid = 4 * sm_count();
   if (steps == 0) {
-    scale_copy_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), per, batch, nsq);
-    return check_launch("scale_copy_kernel");
+    normalize_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), per, batch,
+                                            nsq, ref);
+    return check_launch("normalize_kernel");
   }
 
   const int64_t R = L.R8, C = L.C8, m = L.m, n = L.n;
@@ -529,6 +559,10 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     uint16_t* pin = reinterpret_cast<uint16_t*>(ws + L.off_pin);
     pad_copy_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, pin, R, C, batch);
     if (int st = check_launch("pad_copy_kernel")) return st;
+    if (ref) {
+      normalize_kernel<<<ew_grid, 256, 0, s>>>(pin, pin, xs_elems(L), batch, nsq, 1);
+      if (int st = check_launch("normalize_kernel")) return st;
+    }
     src = pin;
     bufs[0] = reinterpret_cast<uint16_t*>(ws + L.off_w1);
     bufs[1] = reinterpret_cast<uint16_t*>(ws + L.off_w2);
@@ -537,26 +571,34 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     // Step s writes bufs[(steps - 1 - s) & 1] so that the last step lands in `out`.
     bufs[0] = static_cast<uint16_t*>(out);
     bufs[1] = reinterpret_cast<uint16_t*>(ws + L.off_w1);
+    if (ref) {
+      // X0 goes to the buffer that step 0 does not write.
+      uint16_t* x0 = bufs[steps & 1];
+      normalize_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), x0, per, batch, nsq, 1);
+      if (int st = check_launch("normalize_kernel")) return st;
+      src = x0;
+    }
   }
   const float a_ = 3.4445f, b_ = -4.7750f, c_ = 2.0315f;
   for (int st_i = 0; st_i < steps; ++st_i) {
     uint16_t* dst = L.padded ? bufs[st_i & 1] : bufs[(steps - 1 - st_i) & 1];
-    const float* sc = st_i == 0 ? nsq : nullptr;
+    // Fused mode folds 1/(||x|| + 1e-7) into step 0; reference mode normalised X0 above.
+    const float* sc = (!ref && st_i == 0) ? nsq : nullptr;
     int st;
     // A = X X^T (wide orientation): K-major X rows, or MN-major columns of a tall X.
     if (!L.transposed)
-      st = run_gemm(src, 0, xs, src, 0, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, s);
+      st = run_gemm(src, 0, xs, src, 0, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, s);
     else
-      st = run_gemm(src, 1, xs, src, 1, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, s);
+      st = run_gemm(src, 1, xs, src, 1, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, s);
     if (st) return st;
     // B = c (A A) + b A   (A symmetric: A A = A A^T)
-    st = run_gemm(A, 0, gs, A, 0, gs, A, m, gs, B, m, gs, batch, m, m, m, c_, b_, nullptr, 0, 0, 0, s);
+    st = run_gemm(A, 0, gs, A, 0, gs, A, m, gs, B, m, gs, batch, m, m, m, c_, b_, nullptr, 0, 0, 0, ref, s);
     if (st) return st;
     // X' = B X + a X  (tall X: X' = X B + a X with B symmetric)
     if (!L.transposed)
-      st = run_gemm(B, 0, gs, src, 1, xs, src, C, xs, dst, C, xs, batch, m, n, m, 1.f, a_, sc, 1, 1, 1, s);
+      st = run_gemm(B, 0, gs, src, 1, xs, src, C, xs, dst, C, xs, batch, m, n, m, 1.f, a_, sc, 1, 1, 1, ref, s);
     else
-      st = run_gemm(src, 0, xs, B, 0, gs, src, C, xs, dst, C, xs, batch, R, C, C, 1.f, a_, sc, 1, 1, 1, s);
+      st = run_gemm(src, 0, xs, B, 0, gs, src, C, xs, dst, C, xs, batch, R, C, C, 1.f, a_, sc, 1, 1, 1, ref, s);
     if (st) return st;
     src = dst;
   }

@@ -155,10 +155,16 @@ def ns_workspace_bytes(batch: int, rows: int, cols: int) -> int:
     return int(_lib.load().msr_ns_workspace_bytes(batch, rows, cols))
 
 
+NS_REFERENCE_ROUNDING = 0
+NS_FUSED_ROUNDING = 1
+
+
 def newton_schulz(x: torch.Tensor, steps: int = 5, norm_sq: torch.Tensor = None,
-                  out: torch.Tensor = None) -> torch.Tensor:
+                  out: torch.Tensor = None, mode: int = NS_REFERENCE_ROUNDING) -> torch.Tensor:
     """bf16 Newton-Schulz over the last two dims of ``x`` (leading dims are a batch), as
-    ``_newton_schulz(x, steps, out_dtype=None)`` of the reference (muon_sr.py:82-98)."""
+    ``_newton_schulz(x, steps, out_dtype=None)`` of the reference (muon_sr.py:82-98).
+    ``mode`` selects the reference's op-by-op bf16 rounding (default) or one rounding per
+    GEMM (closer to exact arithmetic)."""
     _require(x, "x")
     if x.ndim < 2:
         raise ValueError("Newton-Schulz needs a tensor with ndim >= 2")
@@ -173,13 +179,14 @@ def newton_schulz(x: torch.Tensor, steps: int = 5, norm_sq: torch.Tensor = None,
     if norm_sq is not None:
         _require(norm_sq, "norm_sq", torch.float32)
     _lib.check(_lib.load().msr_newton_schulz_bf16(
-        x.data_ptr(), out.data_ptr(), batch, rows, cols, int(steps),
+        x.data_ptr(), out.data_ptr(), batch, rows, cols, int(steps), int(mode),
         norm_sq.data_ptr() if norm_sq is not None else None, ws.data_ptr(), ws.numel(),
         stream_handle(x.device)), "msr_newton_schulz_bf16")
     return out
 
 
-def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=None, alpha_pow=0, beta_pow=0):
+def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=None, alpha_pow=0, beta_pow=0,
+              ref_rounding=False):
     """Test hook: batched tcgen05 GEMM with the Newton-Schulz epilogue (see the header)."""
     for t, n in ((a, "a"), (b, "b")):
         _require(t, n)
@@ -193,7 +200,7 @@ def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=N
     _lib.check(_lib.load().msr_gemm_bf16(
         a.data_ptr(), int(a_mn_major), b.data_ptr(), int(b_mn_major), c.data_ptr() if c is not None else None,
         d.data_ptr(), batch, M, N, K, float(alpha), float(beta), scale.data_ptr() if scale is not None else None,
-        int(alpha_pow), int(beta_pow), stream_handle(a.device)), "msr_gemm_bf16")
+        int(alpha_pow), int(beta_pow), int(bool(ref_rounding)), stream_handle(a.device)), "msr_gemm_bf16")
     return d
 
 

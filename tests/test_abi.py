@@ -43,7 +43,7 @@ def test_status_strings_and_argument_errors_without_gpu():
     # argument validation happens before any CUDA call
     assert lib.msr_grad_accum_bf16(None, None, -1, 0, 0, None) == 1
     assert b"negative" in lib.msr_last_error()
-    assert lib.msr_newton_schulz_bf16(None, None, 1, 8, 8, 5, None, None, 0, None) == 1
+    assert lib.msr_newton_schulz_bf16(None, None, 1, 8, 8, 5, 0, None, None, 0, None) == 1
     assert lib.msr_ns_workspace_bytes(0, 8, 8) == 0
 
 
