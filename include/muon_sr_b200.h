@@ -67,7 +67,6 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
  *   upd     = nesterov ? g + beta * (new_buf - g) : new_buf
  *   momentum[i] <- SR_bf16(new_buf) with counter (ctr_base + i) mod 2^32
  *   update[i]   <- RNE_bf16(upd)
- *   *norm_sq    += sum_i float(update[i])^2      (if norm_sq != NULL; caller zeroes it)
  * grad and update may alias (the reference prepares in place on its stacked workspace).
  * Replaces _muon_prepare_kernel launches (muon_sr/triton_muon_sr.py:18-50, launched at
  * :94-97 per parameter and :156-159 per shape stack, where ctr_base = index * numel). */
@@ -75,7 +74,6 @@ typedef struct msr_prepare_entry {
   const void* grad;    /* bf16[numel] */
   void* momentum;      /* bf16[numel], updated in place */
   void* update;        /* bf16[numel], output */
-  float* norm_sq;      /* optional fp32 accumulator */
   int64_t numel;
   uint64_t ctr_base;
   uint64_t key;
@@ -176,6 +174,7 @@ size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
 int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows, int64_t cols,
                            int steps, int mode, const float* norm_sq, void* workspace,
                            size_t workspace_bytes, msr_stream_t stream);
+
 
 /* ---- batched bf16 GEMM with the Newton-Schulz epilogue (test hook) --------------------
  * d[b] = alpha_b * (A[b] x B[b]^T) + beta_b * c[b] on the tensor cores, bf16 in/out,

@@ -20,7 +20,7 @@ c_size_t = ctypes.c_size_t
 
 
 class PrepareEntry(ctypes.Structure):
-    _fields_ = [("grad", c_void_p), ("momentum", c_void_p), ("update", c_void_p), ("norm_sq", c_void_p),
+    _fields_ = [("grad", c_void_p), ("momentum", c_void_p), ("update", c_void_p),
                 ("numel", c_int64), ("ctr_base", c_uint64), ("key", c_uint64)]
 
 

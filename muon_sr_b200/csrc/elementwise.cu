@@ -114,30 +114,13 @@ struct PrepareArgs {
 };
 
 __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, float beta, float omb, bool nesterov,
-                                            uint32_t ctr, PhiloxKey key, uint16_t& buf_out, uint16_t& upd_out,
-                                            float& nsq) {
+                                            uint32_t ctr, PhiloxKey key, uint16_t& buf_out, uint16_t& upd_out) {
   const float g = bf16_bits_to_f32(g_bits);
   const float buf = bf16_bits_to_f32(b_bits);
   const float nb = fadd(buf, fmul(omb, fsub(g, buf)));
   const float upd = nesterov ? fadd(g, fmul(beta, fsub(nb, g))) : nb;
   buf_out = sr_bf16_bits(nb, philox_word0(ctr, key));
   upd_out = rne_bf16_bits(upd);
-  const float r = bf16_bits_to_f32(upd_out);
-  nsq = fmaf(r, r, nsq);
-}
-
-__device__ __forceinline__ float block_sum(float v) {
-  __shared__ float red[EW_THREADS / 32];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x >> 5;
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[w] = v;
-  __syncthreads();
-  float s = 0.f;
-  if (threadIdx.x == 0)
-    for (int i = 0; i < EW_THREADS / 32; ++i) s += red[i];
-  return s;
 }
 
 __global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
@@ -153,7 +136,6 @@ __global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_c
     const PhiloxKey key = make_key(E.key);
     const uint64_t cb = E.ctr_base;
     const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
-    float nsq = 0.f;
     if (a.vec[ei]) {
       U16x8 vg[EW_ITERS], vb[EW_ITERS];
 #pragma unroll
@@ -172,14 +154,14 @@ __global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_c
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
             prepare_one(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
-                        static_cast<uint32_t>(cb + static_cast<uint64_t>(idx + j)), key, ob.v[j], ou.v[j], nsq);
+                        static_cast<uint32_t>(cb + static_cast<uint64_t>(idx + j)), key, ob.v[j], ou.v[j]);
           st_u16x8(mb + idx, ob);
           st_u16x8(up + idx, ou);
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t ob, ou;
             prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
-                        ob, ou, nsq);
+                        ob, ou);
             mb[i] = ob;
             up[i] = ou;
           }
@@ -191,15 +173,11 @@ __global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_c
         if (i < n) {
           uint16_t ob, ou;
           prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
-                      ob, ou, nsq);
+                      ob, ou);
           mb[i] = ob;
           up[i] = ou;
         }
       }
-    }
-    if (E.norm_sq != nullptr) {
-      const float s = block_sum(nsq);
-      if (threadIdx.x == 0) atomicAdd(E.norm_sq, s);
     }
   }
 }

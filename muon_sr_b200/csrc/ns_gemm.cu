@@ -388,25 +388,51 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
 // ---------------------------------------------------------------------------------------
 // Small helper kernels of the Newton-Schulz driver
 // ---------------------------------------------------------------------------------------
-// norm_sq[b] += sum of squares of x[b] (caller zeroes norm_sq).
-__global__ void norm_sq_kernel(const uint16_t* __restrict__ x, int64_t per, float* __restrict__ out) {
+// Squared Frobenius norms in two passes with a fixed summation order, so the result is the
+// same bits on every run (data-parallel replicas must agree; float atomics would not).
+constexpr int NORM_THREADS = 256;
+constexpr int NORM_MAX_PARTS = 256;
+
+// Partial sums: parts blocks per matrix (gridDim.x), block i covers a grid-stride share.
+__global__ void __launch_bounds__(NORM_THREADS) norm_partial_kernel(const uint16_t* __restrict__ x, int64_t per,
+                                                                    float* __restrict__ partials) {
   const int64_t b = blockIdx.y;
   const uint16_t* xb = x + b * per;
   float s = 0.f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = blockIdx.x * (int64_t)NORM_THREADS + threadIdx.x; i < per; i += (int64_t)gridDim.x * NORM_THREADS) {
     const float v = bf16_bits_to_f32(xb[i]);
     s = fmaf(v, v, s);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  __shared__ float red[8];
+  __shared__ float red[NORM_THREADS / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
   if (threadIdx.x == 0) {
     float t = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-    atomicAdd(out + b, t);
+    for (int i = 0; i < NORM_THREADS / 32; ++i) t += red[i];
+    partials[b * gridDim.x + blockIdx.x] = t;
   }
+}
+
+// norm_sq[b] = sum of the parts partials of matrix b, one block per matrix.
+__global__ void __launch_bounds__(NORM_MAX_PARTS) norm_final_kernel(const float* __restrict__ partials, int parts,
+                                                                    float* __restrict__ norm_sq) {
+  __shared__ float red[NORM_MAX_PARTS];
+  const int b = blockIdx.x;
+  red[threadIdx.x] = threadIdx.x < parts ? partials[b * parts + threadIdx.x] : 0.f;
+  __syncthreads();
+  for (int w = NORM_MAX_PARTS / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) norm_sq[b] = red[0];
+}
+
+// Blocks per matrix: a function of the shape only (not of the device), so every GPU model
+// sums in the same order.
+inline int norm_parts(int64_t per) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(NORM_MAX_PARTS, (per + 65535) / 65536)));
 }
 
 // dst[b][r][c] (dst dims R2 x C2) = src[b][r][c] for r < R, c < C, else 0 -- or the reverse copy.
@@ -448,7 +474,7 @@ inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 struct NsLayout {
   bool padded, transposed;
   int64_t R8, C8, m, n;
-  size_t off_nsq, off_a, off_b, off_w1, off_w2, off_pin, total;
+  size_t off_nsq, off_part, off_a, off_b, off_w1, off_w2, off_pin, total;
 };
 
 NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
@@ -463,6 +489,7 @@ NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
   const size_t gb = static_cast<size_t>(batch) * L.m * L.m * 2;
   size_t o = 0;
   L.off_nsq = o; o = align256(o + static_cast<size_t>(batch) * 4);
+  L.off_part = o; o = align256(o + static_cast<size_t>(batch) * NORM_MAX_PARTS * 4);
   L.off_a = o;   o = align256(o + gb);
   L.off_b = o;   o = align256(o + gb);
   L.off_w1 = o;  o = align256(o + xb);
@@ -536,10 +563,16 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
   const float* nsq = norm_sq;
   if (nsq == nullptr) {
     float* t = reinterpret_cast<float*>(ws + L.off_nsq);
-    cudaMemsetAsync(t, 0, static_cast<size_t>(batch) * 4, s);
-    const int gx = static_cast<int>(std::min<int64_t>((per + 255) / 256, std::max<int64_t>(1, 4 * sm_count() / batch + 1)));
-    norm_sq_kernel<<<dim3(gx, static_cast<unsigned>(batch)), 256, 0, s>>>(static_cast<const uint16_t*>(x), per, t);
-    if (int st = check_launch("norm_sq_kernel")) return st;
+    float* part = reinterpret_cast<float*>(ws + L.off_part);
+    const int parts = norm_parts(per);
+    for (int64_t b0 = 0; b0 < batch; b0 += 65535) {  // gridDim.y limit
+      const int64_t nb = std::min<int64_t>(65535, batch - b0);
+      norm_partial_kernel<<<dim3(parts, static_cast<unsigned>(nb)), NORM_THREADS, 0, s>>>(
+          static_cast<const uint16_t*>(x) + b0 * per, per, part + b0 * parts);
+      if (int st = check_launch("norm_partial_kernel")) return st;
+    }
+    norm_final_kernel<<<static_cast<unsigned>(batch), NORM_MAX_PARTS, 0, s>>>(part, parts, t);
+    if (int st = check_launch("norm_final_kernel")) return st;
     nsq = t;
   }
   const int ew_grid = 4 * sm_count();

@@ -55,16 +55,15 @@ def grad_accum_(acc: torch.Tensor, grad: torch.Tensor, seed: int, first: bool = 
 
 
 def muon_prepare(items, beta: float, nesterov: bool) -> None:
-    """items: iterable of (grad, momentum, update, norm_sq or None, ctr_base, seed)."""
+    """items: iterable of (grad, momentum, update, ctr_base, seed)."""
     items = list(items)
     if not items:
         return
     arr = (_lib.PrepareEntry * len(items))()
-    for e, (g, buf, upd, nsq, ctr_base, seed) in zip(arr, items):
+    for e, (g, buf, upd, ctr_base, seed) in zip(arr, items):
         e.grad = g.data_ptr()
         e.momentum = buf.data_ptr()
         e.update = upd.data_ptr()
-        e.norm_sq = nsq if isinstance(nsq, int) else (nsq.data_ptr() if nsq is not None else None)
         e.numel = g.numel()
         e.ctr_base = ctr_base & 0xFFFFFFFFFFFFFFFF
         e.key = triton_key(seed)

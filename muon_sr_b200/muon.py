@@ -84,9 +84,8 @@ def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, s
     if p.ndim < 2:
         raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
     update = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
-    nsq = torch.zeros(1, dtype=torch.float32, device=p.device) if p.ndim == 2 else None
-    K.muon_prepare([(grad, buf, update, nsq, 0, seeder(step, param_idx, 0))], beta, nesterov)
-    out = K.newton_schulz(update, ns_steps, norm_sq=nsq)
+    K.muon_prepare([(grad, buf, update, 0, seeder(step, param_idx, 0))], beta, nesterov)
+    out = K.newton_schulz(update, ns_steps)
     K.muon_apply([(p, out, K.ns_scale(p.shape), seeder(step, param_idx, 1))], lr, weight_decay)
 
 
@@ -115,14 +114,13 @@ def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_
             device = stacked_buf.device
             numel = K.numel_of(shape)
             work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=device)
-            nsq = torch.zeros(len(mine), dtype=torch.float32, device=device) if len(shape) == 2 else None
             prep_seed = seeder(step, shape_idx, 0)
-            K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], nsq[j] if nsq is not None else None,
-                             i * numel, prep_seed) for j, i in enumerate(mine)], beta, nesterov)
+            K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
+                            for j, i in enumerate(mine)], beta, nesterov)
             k = max(1, NS_CHUNK_NUMEL // max(1, numel))
             scale = K.ns_scale(shape)
             for s in range(0, len(mine), k):
-                out = K.newton_schulz(work[s:s + k], ns_steps, norm_sq=nsq[s:s + k] if nsq is not None else None)
+                out = K.newton_schulz(work[s:s + k], ns_steps)
                 K.muon_apply([(grp[mine[s + j]], out[j], scale, seeder(step, shape_idx * 10000 + mine[s + j], 1))
                               for j in range(out.shape[0])], lr, weight_decay)
                 del out

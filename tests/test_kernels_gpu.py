@@ -73,13 +73,10 @@ def test_muon_prepare_golden(nest):
     for k, s in enumerate(d["seeds"].tolist()):
         buf = gpu(d["buf"])
         upd = torch.empty_like(buf)
-        nsq = torch.zeros(1, device=DEV)
-        K.muon_prepare([(gpu(d["grad"]), buf, upd, nsq, 0, int(s))], float(d["beta"]), bool(nest))
+        K.muon_prepare([(gpu(d["grad"]), buf, upd, 0, int(s))], float(d["beta"]), bool(nest))
         assert_bits_equal(bits_of(buf), d[f"buf_{nest}_{k}"], "momentum")
         obuf, oupd = ew.muon_prepare(d["grad"], d["buf"], float(d["beta"]), bool(nest), int(s))
         assert_bits_equal(bits_of(upd), oupd, "update (RNE)")
-        want = float((bf16_to_f32(oupd).astype(np.float64) ** 2).sum())
-        assert abs(float(nsq) - want) <= 1e-5 * want
 
 
 def test_muon_prepare_stack_counters_and_multi_entry():
@@ -93,7 +90,7 @@ def test_muon_prepare_stack_counters_and_multi_entry():
     seed = deterministic_seed(12, 3, 0)
     bufs = [gpu(b) for b in bs]
     upds = [torch.empty_like(x) for x in bufs]
-    K.muon_prepare([(gpu(g), b, u, None, base, seed) for g, b, u, base in zip(gs, bufs, upds, bases)], 0.9, True)
+    K.muon_prepare([(gpu(g), b, u, base, seed) for g, b, u, base in zip(gs, bufs, upds, bases)], 0.9, True)
     for g, b, buf, upd, base in zip(gs, bs, bufs, upds, bases):
         ob, ou = ew.muon_prepare(g, b, 0.9, True, seed, ctr_base=base)
         assert_bits_equal(bits_of(buf), ob, f"momentum base {base}")
