@@ -175,6 +175,22 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
                            int steps, int mode, const float* norm_sq, void* workspace,
                            size_t workspace_bytes, msr_stream_t stream);
 
+/* ---- Newton-Schulz without a workspace (no counterpart in the reference) ---------------
+ * For callers that cannot allocate device memory -- e.g. a plugin whose host program owns
+ * every device allocation through its own pool and passes in only input and output
+ * buffers, or a C / FFI caller with no device allocator -- this computes exactly what
+ * msr_newton_schulz_bf16 computes, taking its scratch from a fixed 64 MiB area in the
+ * library's own device memory instead of a workspace. It calls no cudaMalloc / cudaFree.
+ * - Limit: requests with msr_ns_workspace_bytes(batch, rows, cols) > 64 MiB are rejected
+ *   with MSR_ERR_WORKSPACE (e.g. up to a 2048 x 2048 matrix, or 4 of 1024 x 1024).
+ * - Every GPU that loads the library holds the 64 MiB area until the process exits.
+ * - The first call on a device looks up the area's address on that device; make that first
+ *   call before any stream capture.
+ * - All calls share the one area: calls that overlap on the GPU (other streams, other host
+ *   threads without ordering) race and corrupt each other's results. Serialise them. */
+int msr_newton_schulz_bf16_noalloc(const void* x, void* out, int64_t batch, int64_t rows,
+                                   int64_t cols, int steps, int mode, const float* norm_sq,
+                                   msr_stream_t stream);
 
 /* ---- batched bf16 GEMM with the Newton-Schulz epilogue (test hook) --------------------
  * d[b] = alpha_b * (A[b] x B[b]^T) + beta_b * c[b] on the tensor cores, bf16 in/out,

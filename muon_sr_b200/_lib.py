@@ -69,6 +69,8 @@ SIGNATURES = [
     ("msr_ns_workspace_bytes", c_size_t, [c_int64, c_int64, c_int64]),
     ("msr_newton_schulz_bf16", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p,
                                        c_void_p, c_size_t, c_void_p]),
+    ("msr_newton_schulz_bf16_noalloc", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
+                                               c_void_p, c_void_p]),
     ("msr_gemm_bf16", c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                               c_int64, c_float, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
 ]
