@@ -252,8 +252,6 @@ def run_ours(args, rank, world, local_rank):
         a8_bytes_rank = a8_bytes
     a8_gbs = a8_bytes_rank / (a8_kernel_ms * 1e-3) / 1e9 if a8_kernel_ms > 0 else None
     del opt8
-    for p in params:
-        pass
     torch.cuda.empty_cache()
 
     # ---- end to end through the public API with host buffers ----
@@ -355,6 +353,59 @@ def run_reference(args, rank):
             "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_kernel_case(args):
+    """Single-kernel cases for profiling (``--kernel``): a few GB on the device, inputs larger
+    than L2, each kernel launched warmup + steps times; prints per-launch times."""
+    from muon_sr_b200 import kernels as K
+    from muon_sr_b200.adamw8bit import create_dynamic_map
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    out = {"kernel": args.kernel}
+    if args.kernel == "ns":
+        shape = (4, D, D) if args.small else (16, D, D)
+        x = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(0, 1e-3, generator=g)
+        fn = lambda: K.newton_schulz(x, 5)
+        work = shape[0] * ns_flops(shape[1:]) / 1e12
+        unit = "TFLOP/s"
+    else:
+        n = (1 << 28) if args.small else (1 << 30)
+        p = torch.empty(n, dtype=torch.bfloat16, device=dev).normal_(0, 0.02, generator=g)
+        gr = torch.empty_like(p).normal_(0, 1e-3, generator=g)
+        if args.kernel == "adamw8bit":
+            s1 = torch.full((n,), 127, dtype=torch.uint8, device=dev)
+            s2 = torch.zeros(n, dtype=torch.uint8, device=dev)
+            a1 = torch.zeros(n // 256, device=dev)
+            a2 = torch.zeros_like(a1)
+            q1, q2 = create_dynamic_map(True).to(dev), create_dynamic_map(False).to(dev)
+            fn = lambda: K.adamw8bit([(p, gr, s1, s2, a1, a2, 1, 7, True)], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, 256)
+            work = (n * 10 + n // 256 * 16) / 1e9
+        elif args.kernel == "adamw":
+            m, v = torch.zeros_like(p), torch.zeros_like(p)
+            fn = lambda: K.adamw_sr([(p, gr, m, v, 1, 7)], 3e-4, 0.9, 0.95, 1e-10, 0.01)
+            work = n * 14 / 1e9
+        elif args.kernel == "prepare":
+            buf, upd = torch.zeros_like(p), torch.empty_like(p)
+            fn = lambda: K.muon_prepare([(gr, buf, upd, 0, 7)], 0.95, True)
+            work = n * 8 / 1e9
+        else:  # apply
+            upd = torch.empty_like(p).normal_(0, 0.1, generator=g)
+            fn = lambda: K.muon_apply([(p, upd, 1.0, 7)], 0.02, 0.01)
+            work = n * 6 / 1e9
+        unit = "GB/s"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    out.update({"ms_per_call": ms, "rate": work / (ms * 1e-3), "unit": unit, "small": bool(args.small)})
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -363,8 +414,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply"],
+                    help="time one kernel alone (profiling cases) instead of the optimizer step")
+    ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.kernel:
+        run_kernel_case(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
