@@ -197,13 +197,16 @@ int msr_newton_schulz_bf16_noalloc(const void* x, void* out, int64_t batch, int6
  * fp32 accumulate. A is [batch, M, K] (a_mn_major = 0) or [batch, K, M] (1); B is
  * [batch, N, K] (b_mn_major = 0) or [batch, K, N] (1); c, d are [batch, M, N]; c may be
  * NULL. alpha_b = alpha * s^alpha_pow, beta_b = beta * s^beta_pow with s = scale[b]
- * (scale may be NULL). With ref_rounding != 0 the epilogue instead computes
- * bf16(bf16(beta*c) + bf16(alpha*bf16(acc))) (the reference's op-by-op rounding; no scale).
+ * (scale may be NULL). flags: MSR_GEMM_REFERENCE_ROUNDING makes the epilogue compute
+ * bf16(bf16(beta*c) + bf16(alpha*bf16(acc))) (the reference's op-by-op rounding; no scale);
+ * MSR_GEMM_SYMMETRIC (M == N, product known to be symmetric, e.g. A A^T) computes only the
+ * tiles touching the upper triangle and mirror-writes the rest.
  * Rows of every operand must be a multiple of 16 bytes. */
+enum msr_gemm_flags { MSR_GEMM_REFERENCE_ROUNDING = 1, MSR_GEMM_SYMMETRIC = 2 };
+
 int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c,
                   void* d, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha, float beta,
-                  const float* scale, int alpha_pow, int beta_pow, int ref_rounding,
-                  msr_stream_t stream);
+                  const float* scale, int alpha_pow, int beta_pow, int flags, msr_stream_t stream);
 
 #ifdef __cplusplus
 }

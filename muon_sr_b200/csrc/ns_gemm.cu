@@ -55,6 +55,9 @@ struct SharedStorage {
 struct Params {
   int64_t M, N, K, batch;
   int64_t tiles_m, tiles_n, num_tiles;
+  int64_t tiles_per_batch;  // tiles_m * tiles_n, or the upper-triangle count when sym
+  int sym;                  // output is symmetric (M == N): compute tiles touching the upper
+                            // triangle only and mirror-write their strictly-upper part
   uint16_t* d;
   const uint16_t* c;
   int64_t ldd, ldc, d_bstride, c_bstride;
@@ -65,6 +68,29 @@ struct Params {
 };
 
 __device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(rne_bf16_bits(x)); }
+
+// Linear tile index -> (matrix, first row, first column). In symmetric mode row-block i
+// (128 rows) keeps the 256-column tiles k >= i/2, i.e. every tile that holds an element on
+// or above the diagonal; the tiles of a row-block are consecutive, so neighbouring CTAs
+// share A-operand panels.
+__device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t& b, int64_t& m0, int64_t& n0) {
+  b = t / p.tiles_per_batch;
+  int64_t r = t % p.tiles_per_batch;
+  if (!p.sym) {
+    m0 = (r / p.tiles_n) * BM;
+    n0 = (r % p.tiles_n) * BN;
+    return;
+  }
+  int64_t i = 0;
+  for (;;) {
+    const int64_t cnt = p.tiles_n - i / 2;
+    if (r < cnt) break;
+    r -= cnt;
+    ++i;
+  }
+  m0 = i * BM;
+  n0 = (i / 2 + r) * BN;
+}
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
 
@@ -101,7 +127,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem_base = S.tmem_base;
   const int64_t num_kb = (p.K + BK - 1) / BK;
-  const int64_t tiles_per_batch = p.tiles_m * p.tiles_n;
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -111,10 +136,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t issued_mask = 0, last_parity = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        const int32_t b = static_cast<int32_t>(t / tiles_per_batch);
-        const int64_t r = t % tiles_per_batch;
-        const int32_t m0 = static_cast<int32_t>((r / p.tiles_n) * BM);
-        const int32_t n0 = static_cast<int32_t>((r % p.tiles_n) * BN);
+        int64_t b64, m64, n64;
+        decode_tile(p, t, b64, m64, n64);
+        const int32_t b = static_cast<int32_t>(b64);
+        const int32_t m0 = static_cast<int32_t>(m64);
+        const int32_t n0 = static_cast<int32_t>(n64);
         for (int64_t kb = 0; kb < num_kb; ++kb) {
           if (!tc::mbar_wait(&S.empty[stage], phase ^ 1u, abort, WAIT_LIMIT_NS)) {
             record_error(ERR_TMA_WAIT);
@@ -218,10 +244,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc::fence_after_sync();
-      const int64_t b = t / tiles_per_batch;
-      const int64_t r = t % tiles_per_batch;
-      const int64_t m0 = (r / p.tiles_n) * BM;
-      const int64_t n0 = (r % p.tiles_n) * BN;
+      int64_t b, m0, n0;
+      decode_tile(p, t, b, m0, n0);
       float alpha = p.alpha, beta = p.beta;
       if (p.scale != nullptr) {
         float s = p.scale[b];
@@ -283,6 +307,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                   if (col + j < p.N) drow[col + j] = o.v[j];
+              }
+              if (p.sym && col + 7 > row) {
+                // Mirror the strictly-upper elements: (row, c) -> (c, row). Lanes hold
+                // consecutive rows, so each column's stores form one 64-byte segment.
+                uint16_t* dcol = p.d + b * p.d_bstride + row;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int64_t c = col + j;
+                  if (c > row && c < p.N) dcol[c * p.ldd] = o.v[j];
+                }
               }
             }
           }
@@ -362,7 +396,8 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
 int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn, int64_t b_bstride, const void* c,
          int64_t ldc, int64_t c_bstride, void* d, int64_t ldd, int64_t d_bstride, int64_t batch, int64_t M, int64_t N,
          int64_t K, float alpha, float beta, const float* scale, int alpha_pow, int beta_pow, int scale_is_norm_sq,
-         int ref_round, cudaStream_t s) {
+         int ref_round, int sym, cudaStream_t s) {
+  if (sym && M != N) return fail(MSR_ERR_INVALID, "symmetric GEMM needs M == N");
   CUtensorMap ta, tb;
   int st = a_mn ? make_map(&ta, a, M, K, batch, a_bstride, 64) : make_map(&ta, a, K, M, batch, a_bstride, BM);
   if (st) return st;
@@ -372,7 +407,14 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
   p.M = M; p.N = N; p.K = K; p.batch = batch;
   p.tiles_m = (M + BM - 1) / BM;
   p.tiles_n = (N + BN - 1) / BN;
-  p.num_tiles = p.tiles_m * p.tiles_n * batch;
+  p.sym = sym;
+  p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  if (sym) {
+    // row-block i keeps tiles i/2 .. tiles_n-1 (see decode_tile)
+    p.tiles_per_batch = 0;
+    for (int64_t i = 0; i < p.tiles_m; ++i) p.tiles_per_batch += p.tiles_n - i / 2;
+  }
+  p.num_tiles = p.tiles_per_batch * batch;
   p.d = static_cast<uint16_t*>(d);
   p.c = static_cast<const uint16_t*>(c);
   p.ldd = ldd; p.ldc = ldc; p.d_bstride = d_bstride; p.c_bstride = c_bstride;
@@ -451,19 +493,49 @@ __global__ void pad_copy_kernel(const uint16_t* __restrict__ src, int64_t sR, in
 //  ref != 0: out = bf16(x / d), d = bf16(bf16(sqrt(norm_sq)) + 1e-7): the reference's bf16 ops
 //            X / (X.norm() + 1e-7) on a bf16 tensor (muon_sr/muon_sr.py:91).
 //  ref == 0: out = bf16(x * (1 / (sqrt(norm_sq) + 1e-7))) in fp32.
-__global__ void normalize_kernel(const uint16_t* x, uint16_t* out, int64_t per, int64_t batch,
-                                 const float* __restrict__ nsq, int ref) {
-  const int64_t total = per * batch;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const float nrm = sqrtf(nsq[i / per]);
-    const float v = bf16_bits_to_f32(x[i]);
-    if (ref) {
-      const float d = bf16r(__fadd_rn(bf16r(nrm), 1e-7f));
-      out[i] = rne_bf16_bits(__fdiv_rn(v, d));
-    } else {
-      out[i] = rne_bf16_bits(v * (1.0f / (nrm + 1e-7f)));
+// One matrix per blockIdx.y; 8 elements per thread per step when the matrix stride allows
+// 16-byte accesses.
+__device__ __forceinline__ uint16_t normalize_one(uint16_t xb, float d, float s, int ref) {
+  const float v = bf16_bits_to_f32(xb);
+  return ref ? rne_bf16_bits(__fdiv_rn(v, d)) : rne_bf16_bits(v * s);
+}
+
+__global__ void __launch_bounds__(256) normalize_kernel(const uint16_t* x, uint16_t* out, int64_t per,
+                                                        const float* __restrict__ nsq, int ref) {
+  const int64_t b = blockIdx.y;
+  const float nrm = sqrtf(nsq[b]);
+  const float d = bf16r(__fadd_rn(bf16r(nrm), 1e-7f));
+  const float s = 1.0f / (nrm + 1e-7f);
+  const uint16_t* xb = x + b * per;
+  uint16_t* ob = out + b * per;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if ((per & 7) == 0) {
+    for (int64_t v = t0; v < per / 8; v += stride) {
+      U16x8 w = ld_u16x8(xb + v * 8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w.v[j] = normalize_one(w.v[j], d, s, ref);
+      st_u16x8(ob + v * 8, w);
     }
+  } else {
+    for (int64_t i = t0; i < per; i += stride) ob[i] = normalize_one(xb[i], d, s, ref);
   }
+}
+
+// Launches normalize_kernel over `batch` matrices of `per` elements (x may equal out; both
+// 16-byte aligned, which with per % 8 == 0 makes every matrix's vectors aligned).
+int launch_normalize(const uint16_t* x, uint16_t* out, int64_t per, int64_t batch, const float* nsq, int ref,
+                     cudaStream_t s) {
+  const int64_t work = (per & 7) == 0 ? per / 8 : per;
+  const int64_t want = std::max<int64_t>(1, (4 * (int64_t)sm_count() + batch - 1) / batch);
+  const int gx = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, want)));
+  for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+    const int64_t nb = std::min<int64_t>(65535, batch - b0);
+    normalize_kernel<<<dim3(gx, static_cast<unsigned>(nb)), 256, 0, s>>>(x + b0 * per, out + b0 * per, per, nsq + b0,
+                                                                          ref);
+    if (int st = check_launch("normalize_kernel")) return st;
+  }
+  return MSR_OK;
 }
 
 inline int64_t round8(int64_t v) { return (v + 7) / 8 * 8; }
@@ -524,7 +596,7 @@ int msr_device_error(msr_stream_t stream, int clear) {
 
 int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, const void* c, void* d, int64_t batch,
                   int64_t M, int64_t N, int64_t K, float alpha, float beta, const float* scale, int alpha_pow,
-                  int beta_pow, int ref_rounding, msr_stream_t stream) {
+                  int beta_pow, int flags, msr_stream_t stream) {
   if (!a || !b || !d || batch <= 0 || M <= 0 || N <= 0 || K <= 0)
     return fail(MSR_ERR_INVALID, "msr_gemm_bf16: null pointer or non-positive size");
   const int64_t a_inner = a_mn_major ? M : K, b_inner = b_mn_major ? N : K;
@@ -532,8 +604,11 @@ int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, 
     return fail(MSR_ERR_INVALID, "msr_gemm_bf16: contiguous dims must be multiples of 8 (got A %lld, B %lld, N %lld)",
                 (long long)a_inner, (long long)b_inner, (long long)N);
   if (int st = require_sm100()) return st;
+  const int ref = (flags & MSR_GEMM_REFERENCE_ROUNDING) ? 1 : 0;
+  const int sym = (flags & MSR_GEMM_SYMMETRIC) ? 1 : 0;
+  if (sym && M != N) return fail(MSR_ERR_INVALID, "msr_gemm_bf16: MSR_GEMM_SYMMETRIC needs M == N");
   return run_gemm(a, a_mn_major, M * K, b, b_mn_major, N * K, c, N, M * N, d, N, M * N, batch, M, N, K, alpha, beta,
-                  ref_rounding ? nullptr : scale, alpha_pow, beta_pow, 0, ref_rounding ? 1 : 0, to_stream(stream));
+                  ref ? nullptr : scale, alpha_pow, beta_pow, 0, ref, sym, to_stream(stream));
 }
 
 size_t msr_ns_workspace_bytes(int64_t batch, int64_t rows, int64_t cols) {
@@ -576,11 +651,8 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     nsq = t;
   }
   const int ew_grid = 4 * sm_count();
-  if (steps == 0) {
-    normalize_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), per, batch,
-                                            nsq, ref);
-    return check_launch("normalize_kernel");
-  }
+  if (steps == 0)
+    return launch_normalize(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), per, batch, nsq, ref, s);
 
   const int64_t R = L.R8, C = L.C8, m = L.m, n = L.n;
   const int64_t xs = R * C, gs = m * m;
@@ -592,10 +664,8 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     uint16_t* pin = reinterpret_cast<uint16_t*>(ws + L.off_pin);
     pad_copy_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), rows, cols, pin, R, C, batch);
     if (int st = check_launch("pad_copy_kernel")) return st;
-    if (ref) {
-      normalize_kernel<<<ew_grid, 256, 0, s>>>(pin, pin, xs_elems(L), batch, nsq, 1);
-      if (int st = check_launch("normalize_kernel")) return st;
-    }
+    if (ref)
+      if (int st = launch_normalize(pin, pin, xs, batch, nsq, 1, s)) return st;
     src = pin;
     bufs[0] = reinterpret_cast<uint16_t*>(ws + L.off_w1);
     bufs[1] = reinterpret_cast<uint16_t*>(ws + L.off_w2);
@@ -607,8 +677,7 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     if (ref) {
       // X0 goes to the buffer that step 0 does not write.
       uint16_t* x0 = bufs[steps & 1];
-      normalize_kernel<<<ew_grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), x0, per, batch, nsq, 1);
-      if (int st = check_launch("normalize_kernel")) return st;
+      if (int st = launch_normalize(static_cast<const uint16_t*>(x), x0, per, batch, nsq, 1, s)) return st;
       src = x0;
     }
   }
@@ -620,18 +689,18 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
     int st;
     // A = X X^T (wide orientation): K-major X rows, or MN-major columns of a tall X.
     if (!L.transposed)
-      st = run_gemm(src, 0, xs, src, 0, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, s);
+      st = run_gemm(src, 0, xs, src, 0, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, 1, s);
     else
-      st = run_gemm(src, 1, xs, src, 1, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, s);
+      st = run_gemm(src, 1, xs, src, 1, xs, nullptr, m, gs, A, m, gs, batch, m, m, n, 1.f, 0.f, sc, 2, 0, 1, ref, 1, s);
     if (st) return st;
     // B = c (A A) + b A   (A symmetric: A A = A A^T)
-    st = run_gemm(A, 0, gs, A, 0, gs, A, m, gs, B, m, gs, batch, m, m, m, c_, b_, nullptr, 0, 0, 0, ref, s);
+    st = run_gemm(A, 0, gs, A, 0, gs, A, m, gs, B, m, gs, batch, m, m, m, c_, b_, nullptr, 0, 0, 0, ref, 1, s);
     if (st) return st;
     // X' = B X + a X  (tall X: X' = X B + a X with B symmetric)
     if (!L.transposed)
-      st = run_gemm(B, 0, gs, src, 1, xs, src, C, xs, dst, C, xs, batch, m, n, m, 1.f, a_, sc, 1, 1, 1, ref, s);
+      st = run_gemm(B, 0, gs, src, 1, xs, src, C, xs, dst, C, xs, batch, m, n, m, 1.f, a_, sc, 1, 1, 1, ref, 0, s);
     else
-      st = run_gemm(src, 0, xs, B, 0, gs, src, C, xs, dst, C, xs, batch, R, C, C, 1.f, a_, sc, 1, 1, 1, ref, s);
+      st = run_gemm(src, 0, xs, B, 0, gs, src, C, xs, dst, C, xs, batch, R, C, C, 1.f, a_, sc, 1, 1, 1, ref, 0, s);
     if (st) return st;
     src = dst;
   }

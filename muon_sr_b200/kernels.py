@@ -185,7 +185,7 @@ def newton_schulz(x: torch.Tensor, steps: int = 5, norm_sq: torch.Tensor = None,
 
 
 def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=None, alpha_pow=0, beta_pow=0,
-              ref_rounding=False):
+              ref_rounding=False, symmetric=False):
     """Test hook: batched tcgen05 GEMM with the Newton-Schulz epilogue (see the header)."""
     for t, n in ((a, "a"), (b, "b")):
         _require(t, n)
@@ -199,7 +199,8 @@ def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=N
     _lib.check(_lib.load().msr_gemm_bf16(
         a.data_ptr(), int(a_mn_major), b.data_ptr(), int(b_mn_major), c.data_ptr() if c is not None else None,
         d.data_ptr(), batch, M, N, K, float(alpha), float(beta), scale.data_ptr() if scale is not None else None,
-        int(alpha_pow), int(beta_pow), int(bool(ref_rounding)), stream_handle(a.device)), "msr_gemm_bf16")
+        int(alpha_pow), int(beta_pow), (1 if ref_rounding else 0) | (2 if symmetric else 0),
+        stream_handle(a.device)), "msr_gemm_bf16")
     return d
 
 

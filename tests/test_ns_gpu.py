@@ -68,6 +68,22 @@ def test_gemm_reference_rounding_epilogue():
     assert (d.view(torch.int16) == ref.view(torch.int16)).float().mean() > 0.97
 
 
+@pytest.mark.parametrize("shape", [(2, 512, 1024), (3, 1000, 136), (1, 4096, 512), (2, 136, 64), (1, 24, 40)])
+@pytest.mark.parametrize("a_mn", [0, 1])
+def test_gemm_symmetric_mode_equals_full(shape, a_mn):
+    """X X^T computed on upper-triangle tiles + mirror equals the full product bit for bit
+    (the tensor cores sum (r,c) and (c,r) identically), also in the B = c*A*A + b*A form."""
+    batch, m, k = shape
+    x = torch.randn(batch, *((k, m) if a_mn else (m, k)), device=DEV).bfloat16()
+    full = K.gemm_bf16(x, a_mn, x, a_mn, ref_rounding=True)
+    sym = K.gemm_bf16(x, a_mn, x, a_mn, ref_rounding=True, symmetric=True)
+    assert torch.equal(full.view(torch.int16), sym.view(torch.int16))
+    assert torch.equal(sym.view(torch.int16), sym.transpose(1, 2).view(torch.int16))
+    bf = K.gemm_bf16(full, 0, full, 0, full, 2.0315, -4.775, ref_rounding=True)
+    bs = K.gemm_bf16(full, 0, full, 0, full, 2.0315, -4.775, ref_rounding=True, symmetric=True)
+    assert torch.equal(bf.view(torch.int16), bs.view(torch.int16))
+
+
 def test_ns_matches_reference_golden():
     """Against the reference's own outputs, computed on the CPU. The quintic iteration
     amplifies last-bit differences of the fp32 GEMM accumulation (CPU vs tensor cores) to
