@@ -377,7 +377,9 @@ def run_kernel_case(args):
             a1 = torch.zeros(n // 256, device=dev)
             a2 = torch.zeros_like(a1)
             q1, q2 = create_dynamic_map(True).to(dev), create_dynamic_map(False).to(dev)
-            fn = lambda: K.adamw8bit([(p, gr, s1, s2, a1, a2, 1, 7, True)], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, 256)
+            qt = K.quant_tables(q1, q2)
+            fn = lambda: K.adamw8bit([(p, gr, s1, s2, a1, a2, 1, 7, True)], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, 256,
+                                     qtables=qt)
             work = (n * 10 + n // 256 * 16) / 1e9
         elif args.kernel == "adamw":
             m, v = torch.zeros_like(p), torch.zeros_like(p)

@@ -147,7 +147,20 @@ typedef struct msr_adamw8bit_entry {
 typedef struct msr_adamw8bit_hparams {
   float beta1, one_minus_beta1, beta2, one_minus_beta2, decay;
   int32_t block_size;  /* power of two in [32, 4096] */
+  /* Optional quantiser lookup tables for (qmap1, qmap2) in device memory, NULL to run the
+   * reference's 7-step codebook walk. Layout (MSR_QT_* below): uint8 codes[3][MSR_QT_NB]
+   * (signed map x >= 0, signed map x < 0, unsigned map) at offset 0, then float
+   * thresholds[3][256] at offset MSR_QT_T_OFFSET. Bucket of |x| = clamp((bits(|x|) >> 15)
+   * - MSR_QT_BASE, 0, NB - 1); code = codes[s][bucket], then +1 (x >= 0) or -1 (x < 0) if
+   * |x| >= thresholds[s][code]. The Python layer (muon_sr_b200/quant_tables.py) builds and
+   * verifies them against the walk. */
+  const void* qtables;
 } msr_adamw8bit_hparams;
+
+#define MSR_QT_NB 7682
+#define MSR_QT_BASE 24831
+#define MSR_QT_T_OFFSET 23056
+#define MSR_QT_BYTES (MSR_QT_T_OFFSET + 3 * 256 * 4)
 
 int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, const float* qmap1,
                   const float* qmap2, const msr_adamw8bit_hparams* hp, msr_stream_t stream);

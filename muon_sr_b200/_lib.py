@@ -49,7 +49,8 @@ class Adam8Entry(ctypes.Structure):
 
 class Adam8Hparams(ctypes.Structure):
     _fields_ = [("beta1", c_float), ("one_minus_beta1", c_float), ("beta2", c_float),
-                ("one_minus_beta2", c_float), ("decay", c_float), ("block_size", c_int32)]
+                ("one_minus_beta2", c_float), ("decay", c_float), ("block_size", c_int32),
+                ("qtables", c_void_p)]
 
 
 # (name, restype, argtypes) of every exported symbol, in header order.

@@ -46,6 +46,7 @@ class TritonAdamW8bit(Optimizer):
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, block_size=block_size,
                                       min_8bit_size=min_8bit_size, optim_bits=optim_bits))
         self._maps = {}
+        self._qtables = {}
         self._shard = shard
         for group in self.param_groups:
             self._validate_group(group)
@@ -140,8 +141,14 @@ class TritonAdamW8bit(Optimizer):
                     (p, g, state['state1'], state['state2'], state.get('absmax1'), state.get('absmax2'), n, seed,
                      quant))
             for maps, items in by_maps.values():
+                tables = None
+                if maps[0] is not None:
+                    tkey = (maps[0].data_ptr(), maps[1].data_ptr())
+                    if tkey not in self._qtables:  # built once per codebook pair (host copy of 2 KB)
+                        self._qtables[tkey] = K.quant_tables(maps[0], maps[1])
+                    tables = self._qtables[tkey]
                 K.adamw8bit(items, maps[0], maps[1], group['lr'], b1, b2, group['eps'], group['weight_decay'],
-                            group['block_size'])
+                            group['block_size'], qtables=tables)
         if self._shard:
             self._shard.sync_params(self)
         return loss

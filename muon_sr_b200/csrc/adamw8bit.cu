@@ -67,6 +67,33 @@ __device__ __forceinline__ uint32_t quantize(float x, const float* __restrict__ 
   return static_cast<uint32_t>(r) & 0xFFu;
 }
 
+// The same quantiser through the lookup tables (layout in muon_sr_b200.h): the code at
+// the start of |x|'s bucket, moved by one if |x| has reached that code's threshold.
+// codes/T point at one side of one codebook (x >= 0) and, for the signed map, the other.
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t quantize_table(float x, const uint8_t* __restrict__ codes_pos,
+                                                   const float* __restrict__ T_pos,
+                                                   const uint8_t* __restrict__ codes_neg,
+                                                   const float* __restrict__ T_neg) {
+  const uint32_t ab = __float_as_uint(x) & 0x7FFFFFFFu;
+  const int b = min(max(static_cast<int>(ab >> 15) - MSR_QT_BASE, 0), MSR_QT_NB - 1);
+  const float ax = __uint_as_float(ab);
+  if (SIGNED && x < 0.f) {
+    const int c = codes_neg[b];
+    return static_cast<uint32_t>(c - (ax >= T_neg[c] ? 1 : 0));
+  }
+  const int c = codes_pos[b];
+  return static_cast<uint32_t>(c + (ax >= T_pos[c] ? 1 : 0));
+}
+
+// x / d correctly rounded from r = RN(1/d): q = RN(x r), then one residual correction
+// (Markstein's theorem: exact FMA residual + RN(q + rem r) gives RN(x / d)).
+__device__ __forceinline__ float div_by_recip(float x, float d, float r) {
+  const float q = __fmul_rn(x, r);
+  const float rem = __fmaf_rn(-q, d, x);
+  return __fmaf_rn(rem, r, q);
+}
+
 __device__ __forceinline__ bool finite_f(float g) { return fabsf(g) < __int_as_float(0x7f800000); }
 
 // Max-reduce over groups of G consecutive threads (G a power of two, <= Q_THREADS).
@@ -92,18 +119,34 @@ __device__ __forceinline__ float group_max(float v, float* red) {
   }
 }
 
+// Dynamic shared memory: both codebooks, then (TABLES) the lookup tables.
+constexpr size_t smem_for(bool tables) { return 2 * 256 * 4 + (tables ? MSR_QT_BYTES : 0); }
+
 // EPT elements per thread, BS elements per quantisation block.
-template <int BS>
-__global__ __launch_bounds__(Q_THREADS) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
+template <int BS, bool TABLES>
+__global__ __launch_bounds__(Q_THREADS, 2) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
   constexpr int EPT = BS > 2048 ? 16 : 8;
   constexpr int TILE = Q_THREADS * EPT;
   constexpr int G = BS / EPT;  // threads per quantisation block
-  __shared__ float q1[256], q2[256];
+  extern __shared__ __align__(16) uint8_t dsm[];
+  float* q1 = reinterpret_cast<float*>(dsm);
+  float* q2 = q1 + 256;
+  uint8_t* qt = dsm + 2 * 256 * 4;
   __shared__ float red[Q_THREADS / 32];
   for (int i = threadIdx.x; i < 256; i += Q_THREADS) {
     q1[i] = a.qmap1 ? a.qmap1[i] : 0.f;
     q2[i] = a.qmap2 ? a.qmap2[i] : 0.f;
   }
+  if (TABLES) {
+    const uint4* src = static_cast<const uint4*>(a.hp.qtables);
+    for (int i = threadIdx.x; i < MSR_QT_BYTES / 16; i += Q_THREADS) reinterpret_cast<uint4*>(qt)[i] = src[i];
+  }
+  const uint8_t* c_pos1 = qt;
+  const uint8_t* c_neg1 = qt + MSR_QT_NB;
+  const uint8_t* c_pos2 = qt + 2 * MSR_QT_NB;
+  const float* t_pos1 = reinterpret_cast<const float*>(qt + MSR_QT_T_OFFSET);
+  const float* t_neg1 = t_pos1 + 256;
+  const float* t_pos2 = t_pos1 + 512;
   __syncthreads();
   const msr_adamw8bit_hparams hp = a.hp;
   const int64_t total = a.prefix[a.count];
@@ -230,10 +273,21 @@ __global__ __launch_bounds__(Q_THREADS) void adamw8bit_kernel(const __grid_const
       uint32_t c1w[EPT / 4], c2w[EPT / 4];
 #pragma unroll
       for (int j = 0; j < EPT / 4; ++j) { c1w[j] = 0u; c2w[j] = 0u; }
+      const float rm = __frcp_rn(dm), rv = __frcp_rn(dv);
 #pragma unroll
       for (int j = 0; j < EPT; ++j) {
-        c1w[j / 4] |= quantize<true>(__fdiv_rn(m[j], dm), q1) << (8 * (j % 4));
-        c2w[j / 4] |= quantize<false>(__fdiv_rn(v[j], dv), q2) << (8 * (j % 4));
+        const float xm = div_by_recip(m[j], dm, rm);
+        const float xv = div_by_recip(v[j], dv, rv);
+        uint32_t cm, cv;
+        if (TABLES) {
+          cm = quantize_table<true>(xm, c_pos1, t_pos1, c_neg1, t_neg1);
+          cv = quantize_table<false>(xv, c_pos2, t_pos2, nullptr, nullptr);
+        } else {
+          cm = quantize<true>(xm, q1);
+          cv = quantize<false>(xv, q2);
+        }
+        c1w[j / 4] |= cm << (8 * (j % 4));
+        c2w[j / 4] |= cv << (8 * (j % 4));
       }
       if (vec) {
 #pragma unroll
@@ -282,12 +336,23 @@ __global__ __launch_bounds__(Q_THREADS) void adamw8bit_kernel(const __grid_const
   }
 }
 
-template <int BS>
-int launch_bs(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
+template <int BS, bool TABLES>
+int launch_variant(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
   const int64_t cap = static_cast<int64_t>(sm_count()) * Q_BLOCKS_PER_SM;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
-  adamw8bit_kernel<BS><<<grid, Q_THREADS, 0, s>>>(a);
+  constexpr size_t smem = smem_for(TABLES);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  adamw8bit_kernel<BS, TABLES><<<grid, Q_THREADS, smem, s>>>(a);
   return check_launch("adamw8bit_kernel");
+}
+
+template <int BS>
+int launch_bs(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
+  return a.hp.qtables ? launch_variant<BS, true>(a, tiles, s) : launch_variant<BS, false>(a, tiles, s);
 }
 
 inline bool al(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -332,6 +397,8 @@ extern "C" int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, cons
     if (a.count == 0) continue;
     if (any_quant && (qmap1 == nullptr || qmap2 == nullptr))
       return fail(MSR_ERR_INVALID, "msr_adamw8bit: quantized entries need both codebooks");
+    if (hp->qtables != nullptr && (reinterpret_cast<uintptr_t>(hp->qtables) & 15))
+      return fail(MSR_ERR_INVALID, "msr_adamw8bit: qtables must be 16-byte aligned");
     cudaStream_t s = to_stream(stream);
     int st;
     switch (bs) {

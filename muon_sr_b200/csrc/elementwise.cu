@@ -19,7 +19,7 @@ namespace {
 
 constexpr int EW_THREADS = 256;
 constexpr int EW_VEC = 8;
-constexpr int EW_ITERS = 4;
+constexpr int EW_ITERS = 2;
 constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 8192 elements
 constexpr int MAXE = 64;
 constexpr int EW_BLOCKS_PER_SM = 4;
@@ -63,7 +63,7 @@ __global__ __launch_bounds__(EW_THREADS) void grad_accum_first_kernel(uint16_t* 
 }
 
 template <bool VEC>
-__global__ __launch_bounds__(EW_THREADS) void grad_accum_kernel(uint16_t* __restrict__ acc,
+__global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __restrict__ acc,
                                                                const uint16_t* __restrict__ g,
                                                                int64_t n, PhiloxKey key) {
   const int64_t nchunks = (n + EW_CHUNK - 1) / EW_CHUNK;
@@ -123,7 +123,7 @@ __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, fl
   upd_out = rne_bf16_bits(upd);
 }
 
-__global__ __launch_bounds__(EW_THREADS) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
+__global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
   const int64_t total = a.prefix[a.count];
   const bool nesterov = a.nesterov != 0;
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
@@ -201,7 +201,7 @@ __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, 
   return sr_bf16_bits(p, philox_word0(ctr, key));
 }
 
-__global__ __launch_bounds__(EW_THREADS) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
+__global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
@@ -272,7 +272,7 @@ __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uin
   p_bits = sr_bf16_bits(p, philox_word0(ctr, kp));
 }
 
-__global__ __launch_bounds__(EW_THREADS) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
+__global__ __launch_bounds__(EW_THREADS, 2) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);

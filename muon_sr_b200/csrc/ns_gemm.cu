@@ -5,11 +5,11 @@
 // Replaces _newton_schulz (muon_sr/muon_sr.py:82-98), which the reference runs as torch
 // bf16 matmuls (cuBLAS on the GPU) with a separate elementwise op for every term.
 //
-// Kernel layout (one CTA per SM, 256 threads):
-//   warp 0      TMA producer: streams A and B k-blocks (64 deep) into a 4-stage ring
-//   warp 1      TMEM allocator and MMA issuer (one thread issues tcgen05.mma 128x256x16)
-//   warps 4..7  epilogue: tcgen05.ld of the accumulator (lane quarter = warp % 4),
-//               alpha/beta/scale, RNE to bf16, 16-byte global stores
+// Kernel layout (one CTA per SM, 384 threads):
+//   warp 0       TMA producer: streams A and B k-blocks (64 deep) into a 4-stage ring
+//   warp 1       TMEM allocator and MMA issuer (one thread issues tcgen05.mma 128x256x16)
+//   warps 4..11  epilogue: tcgen05.ld of the accumulator (lane quarter = warp % 4, column
+//                half = (warp - 4) / 4), alpha/beta/scale, bf16 rounding, 16-byte stores
 // Two 256-column fp32 accumulators (all 512 TMEM columns) let the epilogue of one tile run
 // under the main loop of the next. Operands are either K-major or MN-major (descriptor bit),
 // which covers X X^T, A A and B X for both orientations of X without any transposes.
@@ -31,7 +31,8 @@ __device__ int g_msr_device_error = 0;
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, UMMA_K = 16;
-constexpr int NUM_THREADS = 256;
+constexpr int NUM_THREADS = 384;  // warps 0-1 TMA/MMA, 4-11 epilogue
+constexpr int EPI_THREADS = 256;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -94,6 +95,76 @@ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t&
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
 
+// One epilogue thread's output row of the current tile.
+struct EpiRow {
+  uint16_t* d;           // output matrix
+  uint16_t* drow;        // its row `row`
+  const uint16_t* crow;  // C operand row, or null when beta * C is not used
+  int64_t row;
+  bool ok;               // row < M
+};
+
+constexpr int EPI_CW = 16;               // columns per epilogue chunk
+constexpr int EPI_G = EPI_CW / 8;         // 16-byte groups per chunk
+
+// C operand for columns [col0, col0 + EPI_CW) of this row (zeros where unused / out of range).
+__device__ __forceinline__ void load_c_chunk(const Params& p, const EpiRow& er, int64_t col0, U16x8 (&cv)[EPI_G]) {
+#pragma unroll
+  for (int g = 0; g < EPI_G; ++g) {
+    const int64_t col = col0 + g * 8;
+    if (er.crow != nullptr && er.ok && col + 8 <= p.N) {
+      cv[g] = ld_u16x8(er.crow + col);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        cv[g].v[j] = (er.crow != nullptr && er.ok && col + j < p.N) ? er.crow[col + j] : uint16_t(0);
+    }
+  }
+}
+
+// Epilogue math and stores for columns [col0, col0 + EPI_CW) of this row.
+__device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, int64_t col0,
+                                            const uint32_t (&v)[EPI_CW], const U16x8 (&cv)[EPI_G], float alpha,
+                                            float beta) {
+  if (!er.ok || col0 >= p.N) return;
+#pragma unroll
+  for (int g = 0; g < EPI_G; ++g) {
+    const int64_t col = col0 + g * 8;
+    if (col >= p.N) break;
+    U16x8 o;
+    if (p.ref_round) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float t = bf16r(__fmul_rn(alpha, bf16r(__uint_as_float(v[g * 8 + j]))));
+        o.v[j] = er.crow != nullptr
+                     ? rne_bf16_bits(__fadd_rn(bf16r(__fmul_rn(beta, bf16_bits_to_f32(cv[g].v[j]))), t))
+                     : rne_bf16_bits(t);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o.v[j] = rne_bf16_bits(fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * bf16_bits_to_f32(cv[g].v[j])));
+    }
+    if (col + 8 <= p.N) {
+      st_u16x8(er.drow + col, o);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (col + j < p.N) er.drow[col + j] = o.v[j];
+    }
+    if (p.sym && col + 7 > er.row) {
+      // Mirror the strictly-upper elements: (row, c) -> (c, row). Lanes hold consecutive
+      // rows, so each column's stores form one 64-byte segment.
+      uint16_t* dcol = er.d + er.row;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t c = col + j;
+        if (c > er.row && c < p.N) dcol[c * p.ldd] = o.v[j];
+      }
+    }
+  }
+}
+
 template <int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
@@ -110,7 +181,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&S.tmem_full[a], 1);
-      tc::mbar_init(&S.tmem_empty[a], 128);
+      tc::mbar_init(&S.tmem_empty[a], EPI_THREADS);
     }
     tc::mbar_init(&S.drain, 1);
     S.abort = 0;
@@ -235,7 +306,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------ epilogue ------------------------------
+    // 8 warps: lane quarter q = warp % 4 (the only TMEM lanes warp q may read) and column
+    // half h of the tile; each warp walks its 4 chunks of 32 columns with the next chunk's
+    // TMEM read and C-operand loads in flight under the current chunk's math.
     const int q = warp & 3;
+    const int h = (warp - 4) >> 2;
+    constexpr int CHUNKS = BN / 2 / EPI_CW;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
@@ -255,71 +331,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const int64_t row = m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
-      uint16_t* drow = p.d + b * p.d_bstride + row * p.ldd;
-      const uint16_t* crow = p.c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
-      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        // tcgen05.ld is warp-collective: every lane issues it, converged, then masks.
-        __syncwarp();
-        uint32_t v[32];
-        tc::tmem_ld_32x32b_x32(tbase + cc * 32, v);
-        tc::tmem_ld_wait();
-        const int64_t col0 = n0 + cc * 32;
-        if (row_ok && col0 < p.N) {
+      const bool use_c = p.c != nullptr && beta != 0.f;
+      EpiRow er;
+      er.d = p.d + b * p.d_bstride;
+      er.drow = er.d + row * p.ldd;
+      er.crow = use_c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
+      er.row = row;
+      er.ok = row_ok;
+      const int64_t cbase = n0 + h * (BN / 2);
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN + h * (BN / 2)) +
+                             (static_cast<uint32_t>(q * 32) << 16);
+      uint32_t v[EPI_CW], vn[EPI_CW];
+      U16x8 cv[EPI_G], cvn[EPI_G];
+      __syncwarp();
+      tc::tmem_ld_32x32b_x16(tbase, v);
+      load_c_chunk(p, er, cbase, cv);
+      tc::tmem_ld_wait();
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int64_t col = col0 + g * 8;
-            if (col < p.N) {
-              float cin[8];
-              const bool full = col + 8 <= p.N;
-              if (crow != nullptr && beta != 0.f) {
-                if (full) {
-                  const U16x8 cv = ld_u16x8(crow + col);
+      for (int cc = 0; cc < CHUNKS; ++cc) {
+        if (cc + 1 < CHUNKS) {
+          __syncwarp();
+          tc::tmem_ld_32x32b_x16(tbase + (cc + 1) * EPI_CW, vn);
+          load_c_chunk(p, er, cbase + (cc + 1) * EPI_CW, cvn);
+        }
+        store_chunk(p, er, cbase + cc * EPI_CW, v, cv, alpha, beta);
+        if (cc + 1 < CHUNKS) {
+          tc::tmem_ld_wait();
 #pragma unroll
-                  for (int j = 0; j < 8; ++j) cin[j] = bf16_bits_to_f32(cv.v[j]);
-                } else {
+          for (int j = 0; j < EPI_CW; ++j) v[j] = vn[j];
 #pragma unroll
-                  for (int j = 0; j < 8; ++j) cin[j] = (col + j < p.N) ? bf16_bits_to_f32(crow[col + j]) : 0.f;
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) cin[j] = 0.f;
-              }
-              U16x8 o;
-              if (p.ref_round) {
-                const bool has_c = crow != nullptr && beta != 0.f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float t = bf16r(__fmul_rn(alpha, bf16r(__uint_as_float(v[g * 8 + j]))));
-                  o.v[j] = has_c ? rne_bf16_bits(__fadd_rn(bf16r(__fmul_rn(beta, cin[j])), t)) : rne_bf16_bits(t);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float accv = __uint_as_float(v[g * 8 + j]);
-                  o.v[j] = rne_bf16_bits(fmaf(alpha, accv, beta * cin[j]));
-                }
-              }
-              if (full) {
-                st_u16x8(drow + col, o);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                  if (col + j < p.N) drow[col + j] = o.v[j];
-              }
-              if (p.sym && col + 7 > row) {
-                // Mirror the strictly-upper elements: (row, c) -> (c, row). Lanes hold
-                // consecutive rows, so each column's stores form one 64-byte segment.
-                uint16_t* dcol = p.d + b * p.d_bstride + row;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const int64_t c = col + j;
-                  if (c > row && c < p.N) dcol[c * p.ldd] = o.v[j];
-                }
-              }
-            }
-          }
+          for (int j = 0; j < EPI_G; ++j) cv[j] = cvn[j];
         }
       }
       __syncwarp();

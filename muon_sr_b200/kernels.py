@@ -109,8 +109,25 @@ def adamw_sr(items, lr: float, beta1: float, beta2: float, eps: float, weight_de
     _lib.check(_lib.load().msr_adamw_sr(arr, len(items), ctypes.byref(hp), stream_handle(dev)), "msr_adamw_sr")
 
 
-def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_size) -> None:
-    """items: iterable of (param, grad, state1, state2, absmax1, absmax2, step, seed, quantized)."""
+_qtable_cache = {}
+
+
+def quant_tables(qmap1: torch.Tensor, qmap2: torch.Tensor):
+    """Device copy of the quantiser lookup tables for this codebook pair (built once per
+    device and codebook contents), or None if the table rule is not exact for them."""
+    from . import quant_tables as qt
+    q1 = qmap1.detach().float().cpu().numpy()
+    q2 = qmap2.detach().float().cpu().numpy()
+    key = (qmap1.device.index, q1.tobytes(), q2.tobytes())
+    if key not in _qtable_cache:
+        b = qt.blob(q1, q2)
+        _qtable_cache[key] = None if b is None else torch.from_numpy(b).to(qmap1.device)
+    return _qtable_cache[key]
+
+
+def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_size, qtables=None) -> None:
+    """items: iterable of (param, grad, state1, state2, absmax1, absmax2, step, seed, quantized).
+    ``qtables``: the lookup-table blob of ``quant_tables`` (None runs the codebook walk)."""
     items = list(items)
     if not items:
         return
@@ -128,7 +145,8 @@ def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_si
         e.sqrt_bc2_eps = float(f32(sq_bc2 * eps32))
         e.quantized = 1 if quant else 0
     hp = _lib.Adam8Hparams(float(f32(beta1)), float(f32(1.0 - beta1)), float(f32(beta2)), float(f32(1.0 - beta2)),
-                           float(f32(1.0 - lr * weight_decay)), int(block_size))
+                           float(f32(1.0 - lr * weight_decay)), int(block_size),
+                           qtables.data_ptr() if qtables is not None else None)
     dev = items[0][0].device
     _lib.check(_lib.load().msr_adamw8bit(arr, len(items), _ptr(qmap1), _ptr(qmap2), ctypes.byref(hp),
                                          stream_handle(dev)), "msr_adamw8bit")

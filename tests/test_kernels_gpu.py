@@ -132,10 +132,13 @@ def test_adamw_golden():
         assert_bits_equal(bits_of(v), d[f"ev_{k}"], "v edge")
 
 
-def _adam8_run(case):
+def _adam8_run(case, tables):
     d = load("adamw8bit.npz")
     n, block, quant = d[f"c{case}_meta"].tolist()
     q1, q2 = torch.from_numpy(d["qmap1"]).to(DEV), torch.from_numpy(d["qmap2"]).to(DEV)
+    qt = K.quant_tables(q1, q2) if tables else None
+    if tables:
+        assert qt is not None
     p = gpu(d[f"c{case}_p0"])
     if quant:
         s1 = torch.full((n,), 127, dtype=torch.uint8, device=DEV)
@@ -149,7 +152,7 @@ def _adam8_run(case):
     for step in (1, 2, 3):
         seed = int(d[f"c{case}_seed{step}"])
         K.adamw8bit([(p, gpu(d[f"c{case}_g{step}"]), s1, s2, a1, a2, step, seed, bool(quant))], q1, q2,
-                    1e-3, 0.9, 0.999, 1e-8, 0.01, block)
+                    1e-3, 0.9, 0.999, 1e-8, 0.01, block, qtables=qt)
         assert_bits_equal(bits_of(p), d[f"c{case}_p{step}"], f"p step {step}")
         if quant:
             assert_bits_equal(s1.cpu().numpy(), d[f"c{case}_s1_{step}"], f"codes1 step {step}")
@@ -161,16 +164,19 @@ def _adam8_run(case):
             assert_bits_equal(bits_of(s2), d[f"c{case}_s2_{step}"], f"v step {step}")
 
 
+@pytest.mark.parametrize("tables", [False, True])
 @pytest.mark.parametrize("case", [0, 1, 2, 3])
-def test_adamw8bit_golden(case):
-    _adam8_run(case)
+def test_adamw8bit_golden(case, tables):
+    _adam8_run(case, tables)
 
 
+@pytest.mark.parametrize("tables", [False, True])
 @pytest.mark.parametrize("block", [32, 64, 128, 256, 512, 1024, 2048, 4096])
-def test_adamw8bit_block_sizes_vs_oracle(block):
+def test_adamw8bit_block_sizes_vs_oracle(block, tables):
     rng = np.random.default_rng(block)
     Q1, Q2 = o8.create_dynamic_map(True), o8.create_dynamic_map(False)
     q1, q2 = torch.from_numpy(Q1).to(DEV), torch.from_numpy(Q2).to(DEV)
+    qt = K.quant_tables(q1, q2) if tables else None
     for n in (block * 3 + 5, 9000):
         pb = rne_bf16((rng.standard_normal(n) * 0.02).astype(np.float32))
         s1 = np.full(n, 127, np.uint8); s2 = np.zeros(n, np.uint8)
@@ -182,7 +188,8 @@ def test_adamw8bit_block_sizes_vs_oracle(block):
             seed = deterministic_seed(step, 9)
             pb, s1, s2, a1, a2 = o8.adamw8bit(pb, gb, s1, s2, a1, a2, Q1, Q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, step,
                                               seed, block, True)
-            K.adamw8bit([(P, gpu(gb), S1, S2, A1, A2, step, seed, True)], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, block)
+            K.adamw8bit([(P, gpu(gb), S1, S2, A1, A2, step, seed, True)], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, block,
+                        qtables=qt)
             assert_bits_equal(bits_of(P), pb, f"p block {block} n {n}")
             assert_bits_equal(S1.cpu().numpy(), s1, "codes1")
             assert_bits_equal(S2.cpu().numpy(), s2, "codes2")
