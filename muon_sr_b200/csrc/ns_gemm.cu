@@ -70,27 +70,61 @@ struct Params {
 
 __device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(rne_bf16_bits(x)); }
 
-// Linear tile index -> (matrix, first row, first column). In symmetric mode row-block i
-// (128 rows) keeps the 256-column tiles k >= i/2, i.e. every tile that holds an element on
-// or above the diagonal; the tiles of a row-block are consecutive, so neighbouring CTAs
-// share A-operand panels.
+// Tile rasterisation: row-blocks (128 rows) are taken in bands of GROUP_M; inside a band
+// the tiles run column by column, rows fastest, so the ~148 tiles of one wave touch about
+// GROUP_M A-panels and 148 / GROUP_M B-panels and both stay in L2.
+constexpr int64_t GROUP_M = 8;
+
+// Symmetric mode keeps, in row-block i, the 256-column tiles k >= i/2 (every tile holding
+// an element on or above the diagonal). In a band starting at row-block g0 (even), column
+// k = g0/2 + d holds the band's first min(R, 2d + 2) row-blocks (R = rows in the band).
+__device__ __forceinline__ int64_t sym_band_tiles(int64_t R, int64_t D) {
+  // sum_{d < D} min(R, 2d + 2): the ramp d < R/2 - 1 ... plus full columns
+  const int64_t ramp = R / 2;  // columns with 2d + 2 < R (R even) or <= R (R odd, last band)
+  int64_t s = 0;
+  const int64_t dr = D < ramp ? D : ramp;
+  s += dr * (dr + 1);                       // sum of 2d + 2 for d < dr
+  if (D > dr) s += (D - dr) * R;
+  return s;
+}
+
+// Linear tile index -> (matrix, first row, first column).
 __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t& b, int64_t& m0, int64_t& n0) {
   b = t / p.tiles_per_batch;
   int64_t r = t % p.tiles_per_batch;
   if (!p.sym) {
-    m0 = (r / p.tiles_n) * BM;
-    n0 = (r % p.tiles_n) * BN;
+    const int64_t band_tiles = GROUP_M * p.tiles_n;
+    const int64_t g0 = (r / band_tiles) * GROUP_M;
+    const int64_t R = min(GROUP_M, p.tiles_m - g0);
+    const int64_t w = r % band_tiles;
+    m0 = (g0 + w % R) * BM;
+    n0 = (w / R) * BN;
     return;
   }
-  int64_t i = 0;
+  int64_t g0 = 0;
   for (;;) {
-    const int64_t cnt = p.tiles_n - i / 2;
+    const int64_t R = min(GROUP_M, p.tiles_m - g0);
+    const int64_t cnt = sym_band_tiles(R, p.tiles_n - g0 / 2);
     if (r < cnt) break;
     r -= cnt;
-    ++i;
+    g0 += GROUP_M;
   }
-  m0 = i * BM;
-  n0 = (i / 2 + r) * BN;
+  const int64_t R = min(GROUP_M, p.tiles_m - g0);
+  // column offset d: prefix over the ramp d*(d+1) (rows 2d+2 each), then R per column
+  int64_t d = 0, rows_d = 0;
+  for (;;) {
+    rows_d = min(R, 2 * d + 2);
+    if (r < rows_d) break;
+    r -= rows_d;
+    ++d;
+    if (rows_d == R) {  // past the ramp: every further column holds all R rows
+      d += r / R;
+      r %= R;
+      break;
+    }
+  }
+  m0 = (g0 + r) * BM;
+  n0 = (g0 / 2 + d) * BN;
 }
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
