@@ -90,7 +90,7 @@ def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, s
 
 
 def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
-                    seeder, owner=None):
+                    seeder, owner=None, share=None):
     """Batched step over shape stacks (``_triton_muon_batch_step``, triton_muon_sr.py:128-177).
 
     Prepare runs once per stack with seed S(step, shape_idx, 0) and counters running over the
@@ -98,40 +98,48 @@ def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_
     S(step, shape_idx * 10000 + i, 1). A stack where only some parameters have gradients
     falls back to per-parameter steps with param_idx = shape_idx * 10000 + i.
     ``owner(shape_idx, i) -> bool`` restricts the work to this rank's matrices; seeds and
-    counters stay global, so results do not depend on the number of ranks.
+    counters stay global, so results do not depend on the number of ranks. ``share(params)``
+    is called after each stack so its weights can travel while the next stack computes.
     """
     for shape_idx, (shape, grp) in enumerate(shape_groups.items()):
-        active = [p for p in grp if p.grad is not None]
-        if not active:
-            continue
-        stacked_buf = stacked_bufs[shape]
-        if len(active) == len(grp):
-            mine = [i for i in range(len(grp)) if owner is None or owner(shape_idx, i)]
-            if not mine:
-                continue
-            if len(shape) < 2:
-                raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
-            device = stacked_buf.device
-            numel = K.numel_of(shape)
-            work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=device)
-            prep_seed = seeder(step, shape_idx, 0)
-            K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
-                            for j, i in enumerate(mine)], beta, nesterov)
-            k = max(1, NS_CHUNK_NUMEL // max(1, numel))
-            scale = K.ns_scale(shape)
-            for s in range(0, len(mine), k):
-                out = K.newton_schulz(work[s:s + k], ns_steps)
-                K.muon_apply([(grp[mine[s + j]], out[j], scale, seeder(step, shape_idx * 10000 + mine[s + j], 1))
-                              for j in range(out.shape[0])], lr, weight_decay)
-                del out
-            del work
-        else:
-            for p in active:
-                i = buf_indices[id(p)]
-                if owner is not None and not owner(shape_idx, i):
-                    continue
+        _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay,
+                    step, seeder, owner)
+        if share is not None:
+            share(grp)
+
+
+def _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
+                seeder, owner):
+    """One shape stack of ``muon_batch_step``."""
+    active = [p for p in grp if p.grad is not None]
+    if not active:
+        return
+    stacked_buf = stacked_bufs[shape]
+    if len(active) < len(grp):
+        for p in active:
+            i = buf_indices[id(p)]
+            if owner is None or owner(shape_idx, i):
                 muon_single_step(p, _grad_of(p), stacked_buf[i], beta, nesterov, ns_steps, lr, weight_decay,
                                  step, shape_idx * 10000 + i, seeder)
+        return
+    mine = [i for i in range(len(grp)) if owner is None or owner(shape_idx, i)]
+    if not mine:
+        return
+    if len(shape) < 2:
+        raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
+    numel = K.numel_of(shape)
+    work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=stacked_buf.device)
+    prep_seed = seeder(step, shape_idx, 0)
+    K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
+                    for j, i in enumerate(mine)], beta, nesterov)
+    k = max(1, NS_CHUNK_NUMEL // max(1, numel))
+    scale = K.ns_scale(shape)
+    for s in range(0, len(mine), k):
+        out = K.newton_schulz(work[s:s + k], ns_steps)
+        K.muon_apply([(grp[mine[s + j]], out[j], scale, seeder(step, shape_idx * 10000 + mine[s + j], 1))
+                      for j in range(out.shape[0])], lr, weight_decay)
+        del out
+    del work
 
 
 def _check_params(params, name):
@@ -197,7 +205,7 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
                         self.state[p]["step"] = self._global_step
                 owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
                 muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd, step,
-                                seeder, owner)
+                                seeder, owner, self._shard.share if self._shard else None)
             else:
                 for param_idx, p in enumerate(group["params"]):
                     assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
@@ -216,6 +224,8 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
                         continue
                     muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
                                      state.get("step", 0), param_idx, seeder)
+                if self._shard:
+                    self._shard.share(group["params"])
         if self._shard:
             self._shard.sync_params(self)
         return loss
@@ -271,10 +281,18 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
         name = type(self).__name__
         if self._shard:
             self._shard.bind(self)
-        param_offset = 0
-        for gi, group in enumerate(self.param_groups):
-            group_offset = param_offset
-            param_offset += len(group["params"])
+        offsets, total = [], 0
+        for group in self.param_groups:
+            offsets.append(total)
+            total += len(group["params"])
+        order = list(range(len(self.param_groups)))
+        if self._shard:
+            # AdamW groups (embedding, head) first so their broadcasts overlap the Muon work;
+            # every group's math is independent of the processing order.
+            order.sort(key=lambda gi: bool(self.param_groups[gi]["use_muon"]))
+        for gi in order:
+            group = self.param_groups[gi]
+            group_offset = offsets[gi]
             if group["use_muon"]:
                 lr, wd = group["lr"], group["weight_decay"]
                 beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
@@ -298,7 +316,7 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                             self.state[p]["step"] = self._global_step
                     owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
                     muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd,
-                                    step, seeder, owner)
+                                    step, seeder, owner, self._shard.share if self._shard else None)
                 else:
                     for param_idx, p in enumerate(group["params"]):
                         assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
@@ -317,6 +335,8 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                             continue
                         muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
                                          state.get("step", 0), param_idx, seeder)
+                    if self._shard:
+                        self._shard.share(group["params"])
             else:
                 lr = group["lr"]
                 beta1, beta2 = group["betas"]
@@ -339,6 +359,8 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                     items.append((p, _grad_of(p), state["ema"], state["ema_squared"], state["step"],
                                   seeder(state["step"], group_offset + i, 0)))
                 K.adamw_sr(items, lr, beta1, beta2, eps, wd)
+                if self._shard:
+                    self._shard.share(group["params"])
         if self._shard:
             self._shard.sync_params(self)
         return loss

@@ -10,9 +10,9 @@ NCCL (NVLink / NVSwitch), so the step's work is divided by the number of ranks.
   for Muon matrices, bytes at the HBM rate for AdamW / 8-bit tensors.
 * Seeds and Philox counters stay global, so every rank writes exactly the bits a single GPU
   would (Newton-Schulz computes each matrix independently of how the batch is chunked).
-* Sharing: after the step every updated parameter is broadcast from its owner; the NCCL
-  calls are enqueued after the kernels on the current stream and overlap nothing else in
-  this version.
+* Sharing: as soon as a shape stack (or param group) is updated, its parameters are
+  broadcast from their owners on NCCL's stream, so the transfers run under the next
+  stacks' Newton-Schulz work; the step ends by waiting for all of them.
 * Optimizer state (momentum, moments) stays with the owner; ``state_dict()`` on a rank holds
   valid values only for the parameters that rank owns.
 """
@@ -90,6 +90,7 @@ class Sharder:
     def bind(self, optimizer):
         self._ensure(optimizer)
         self._groups = optimizer.param_groups
+        self.begin_step()
         return self
 
     def owns(self, gi, pi) -> bool:
@@ -100,14 +101,30 @@ class Sharder:
         return lambda shape_idx, i: self._owner[id(stacks[shape_idx][i])] == self.rank
 
     # -- weight sharing ----------------------------------------------------------------------
-    def sync_params(self, optimizer):
-        """Broadcast every parameter that has a gradient from its owner to all ranks."""
-        works = []
-        for p in self._order:
-            if p.grad is None:
+    def share(self, params):
+        """Start broadcasting each of ``params`` that has a gradient from its owner. Every
+        rank must call this with the same tensors in the same order (the optimizers call it
+        once per shape stack / param group, in a fixed order). The broadcasts are enqueued
+        behind the kernels already issued on the current stream and run while later work
+        proceeds; ``sync_params`` waits for them."""
+        if not hasattr(self, "_pending"):
+            self._pending = []
+        for p in params:
+            if p.grad is None or id(p) in self._shared:
                 continue
+            self._shared.add(id(p))
             src = self._owner[id(p)]
             src_global = dist.get_global_rank(self.group, src) if self.group is not None else src
-            works.append(dist.broadcast(p.data, src=src_global, group=self.group, async_op=True))
-        for w in works:
+            self._pending.append(dist.broadcast(p.data, src=src_global, group=self.group, async_op=True))
+
+    def begin_step(self):
+        self._shared = set()
+        self._pending = []
+
+    def sync_params(self, optimizer):
+        """Share whatever was not shared yet, then make the current stream wait for all of
+        this step's broadcasts."""
+        self.share(self._order)
+        for w in self._pending:
             w.wait()
+        self._pending = []
