@@ -124,7 +124,7 @@ constexpr size_t smem_for(bool tables) { return 2 * 256 * 4 + (tables ? MSR_QT_B
 
 // EPT elements per thread, BS elements per quantisation block.
 template <int BS, bool TABLES>
-__global__ __launch_bounds__(Q_THREADS, 2) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
+__global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
   constexpr int EPT = BS > 2048 ? 16 : 8;
   constexpr int TILE = Q_THREADS * EPT;
   constexpr int G = BS / EPT;  // threads per quantisation block
