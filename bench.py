@@ -186,7 +186,7 @@ def run_ours(args, rank, world, local_rank):
     lib = _lib.load()
     hbm_gbs, tf_burst, tf_sus, peak_kind = peaks()
     muon, adam = build_tensors(device)
-    shard = Sharder() if world > 1 else None
+    shard = Sharder(reserve_sms=args.reserve_sms) if world > 1 else None
     opt = TritonMuonSRWithAuxAdam([
         dict(params=muon, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
         dict(params=adam, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
@@ -419,6 +419,8 @@ def main():
     ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply"],
                     help="time one kernel alone (profiling cases) instead of the optimizer step")
     ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
+    ap.add_argument("--reserve-sms", type=int, default=int(os.environ.get("MSR_RESERVE_SMS", "0")),
+                    help="N>1: SMs the GEMMs leave to the concurrent weight broadcasts")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.kernel:

@@ -46,6 +46,10 @@ const char* msr_last_error(void);
 int msr_device_error(msr_stream_t stream, int clear);
 /* Number of kernels this library has launched in this process (all threads, all devices). */
 uint64_t msr_launch_count(void);
+/* Caps the number of CTAs (one per SM) of the persistent GEMM kernels; 0 = one per SM (the
+ * default). A caller that runs collectives concurrently with the optimizer step (e.g. the
+ * sharded step's weight broadcasts) leaves SMs free for them this way. Process-wide. */
+void msr_set_gemm_max_ctas(int max_ctas);
 
 /* ---- Philox (test hook) ------------------------------------------------------------
  * out[i] = word 0 of Philox4x32-10 with counter ((ctr_base + i) mod 2^32, 0, 0, 0) and key

@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 namespace msr {
@@ -455,12 +456,17 @@ int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, i
 
 size_t smem_bytes() { return sizeof(SharedStorage) + 1024; }
 
+std::atomic<int> g_gemm_max_ctas{0};
+
 template <int A_MN, int B_MN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
   auto kern = gemm_kernel<A_MN, B_MN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
   if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, sm_count()));
+  int ctas = sm_count();
+  const int cap = g_gemm_max_ctas.load(std::memory_order_relaxed);
+  if (cap > 0 && cap < ctas) ctas = cap;
+  const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, ctas));
   kern<<<grid, NUM_THREADS, smem_bytes(), s>>>(ta, tb, p);
   return check_launch("gemm_kernel");
 }
@@ -655,6 +661,8 @@ using namespace msr;
 using namespace msr::gemm;
 
 extern "C" {
+
+void msr_set_gemm_max_ctas(int max_ctas) { g_gemm_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
 
 int msr_device_error(msr_stream_t stream, int clear) {
   cudaError_t e = cudaStreamSynchronize(to_stream(stream));

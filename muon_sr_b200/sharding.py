@@ -44,12 +44,19 @@ def _cost(p, use_muon, ns_steps):
 class Sharder:
     """Spreads the per-parameter optimizer work of one optimizer over a process group."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, reserve_sms: int = 0):
+        """``reserve_sms``: SMs the Newton-Schulz GEMMs leave free so that the weight
+        broadcasts (NCCL kernels) run concurrently with them (pair it with
+        NCCL_MAX_NCHANNELS <= reserve_sms); 0 keeps every SM for the GEMMs."""
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("Sharder needs an initialised torch.distributed process group")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        if reserve_sms > 0 and torch.cuda.is_available():
+            from . import _lib
+            sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+            _lib.load().msr_set_gemm_max_ctas(max(1, sms - int(reserve_sms)))
         self._owner = None  # id(param) -> rank within the group
         self._order = None  # params in a fixed order for the broadcasts
 
