@@ -209,6 +209,27 @@ int msr_newton_schulz_bf16_noalloc(const void* x, void* out, int64_t batch, int6
                                    int64_t cols, int steps, int mode, const float* norm_sq,
                                    msr_stream_t stream);
 
+/* ---- peer mappings for the sharded step (no counterpart in the single-device reference) --
+ * The sharded optimizer (several ranks on one node, each updating the parameters it owns)
+ * shares the updated bf16 weights with copy-engine peer copies over NVLink:
+ * msr_ipc_export gives the 64-byte IPC handle of the device allocation holding ptr and ptr's
+ * offset in it; msr_ipc_import maps such an allocation of another process (peer access is
+ * enabled lazily); msr_ipc_close unmaps it; msr_copy_async enqueues one cudaMemcpyAsync
+ * (peer-to-peer when the pointers live on different devices). Requires cudaMalloc'd
+ * memory (not VMM / expandable segments). */
+int msr_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+int msr_ipc_import(const void* handle, void** base_out);
+int msr_ipc_close(void* base);
+int msr_copy_async(void* dst, const void* src, size_t bytes, msr_stream_t stream);
+/* Interprocess events ordering those copies: create (on the current device) and export a
+ * 64-byte handle; open a peer's handle in the current device's context; record on / wait
+ * from a stream; destroy. Events are opaque cudaEvent_t handles. */
+int msr_ipc_event_create(void** event_out, void* handle_out);
+int msr_ipc_event_open(const void* handle, void** event_out);
+int msr_event_record(void* event, msr_stream_t stream);
+int msr_stream_wait_event(msr_stream_t stream, void* event);
+int msr_event_destroy(void* event);
+
 /* ---- batched bf16 GEMM with the Newton-Schulz epilogue (test hook) --------------------
  * d[b] = alpha_b * (A[b] x B[b]^T) + beta_b * c[b] on the tensor cores, bf16 in/out,
  * fp32 accumulate. A is [batch, M, K] (a_mn_major = 0) or [batch, K, M] (1); B is

@@ -73,6 +73,15 @@ SIGNATURES = [
                                        c_void_p, c_size_t, c_void_p]),
     ("msr_newton_schulz_bf16_noalloc", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                                c_void_p, c_void_p]),
+    ("msr_ipc_export", c_int, [c_void_p, c_void_p, ctypes.POINTER(c_uint64)]),
+    ("msr_ipc_import", c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    ("msr_ipc_close", c_int, [c_void_p]),
+    ("msr_copy_async", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("msr_ipc_event_create", c_int, [ctypes.POINTER(c_void_p), c_void_p]),
+    ("msr_ipc_event_open", c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    ("msr_event_record", c_int, [c_void_p, c_void_p]),
+    ("msr_stream_wait_event", c_int, [c_void_p, c_void_p]),
+    ("msr_event_destroy", c_int, [c_void_p]),
     ("msr_gemm_bf16", c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                               c_int64, c_float, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
 ]

@@ -16,6 +16,7 @@ NCCL (NVLink / NVSwitch), so the step's work is divided by the number of ranks.
 * Optimizer state (momentum, moments) stays with the owner; ``state_dict()`` on a rank holds
   valid values only for the parameters that rank owns.
 """
+import ctypes
 import heapq
 
 import torch
@@ -42,14 +43,30 @@ def _cost(p, use_muon, ns_steps):
 
 
 class Sharder:
-    """Spreads the per-parameter optimizer work of one optimizer over a process group."""
+    """Spreads the per-parameter optimizer work of one optimizer over a process group.
 
-    def __init__(self, group=None, reserve_sms: int = 0):
-        """``reserve_sms``: SMs the Newton-Schulz GEMMs leave free so that the weight
-        broadcasts (NCCL kernels) run concurrently with them (pair it with
-        NCCL_MAX_NCHANNELS <= reserve_sms); 0 keeps every SM for the GEMMs."""
+    Weight sharing (``transport``):
+
+    * ``"p2p"`` (default on CUDA): every rank maps, once, the device allocations that hold
+      the parameters other ranks own (CUDA IPC) and pulls their updated values with
+      copy-engine peer copies over NVLink on one side stream per owner, so the transfers use
+      no SMs and run under the Newton-Schulz GEMMs. Ordering: after each shape stack every
+      rank records an interprocess event on its compute stream, a host-only (gloo) barrier
+      makes sure all records are enqueued, and the copies wait on the owners' events; at the
+      end of the step the compute stream waits for the copies and for the peers' copies of
+      this rank's weights (another event + barrier), so the next step's updates cannot
+      overwrite weights a peer is still reading. Falls back to ``"nccl"`` when the memory
+      cannot be mapped (e.g. VMM / expandable-segment allocations).
+    * ``"nccl"``: one NCCL broadcast per parameter from its owner.
+    """
+
+    def __init__(self, group=None, reserve_sms: int = 0, transport: str = "p2p"):
+        """``reserve_sms``: SMs the Newton-Schulz GEMMs leave free for concurrent NCCL
+        kernels (pair it with NCCL_MAX_NCHANNELS <= reserve_sms); 0 keeps every SM."""
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("Sharder needs an initialised torch.distributed process group")
+        if transport not in ("p2p", "nccl"):
+            raise ValueError("transport must be 'p2p' or 'nccl'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -57,8 +74,12 @@ class Sharder:
             from . import _lib
             sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
             _lib.load().msr_set_gemm_max_ctas(max(1, sms - int(reserve_sms)))
+        self.transport = transport if torch.cuda.is_available() else "nccl"
+        # host-only barriers for the p2p ordering (created collectively, same order on all ranks)
+        self._host = dist.new_group(backend="gloo") if self.transport == "p2p" else None
         self._owner = None  # id(param) -> rank within the group
-        self._order = None  # params in a fixed order for the broadcasts
+        self._order = None  # params in a fixed order
+        self._p2p = None    # lazily built peer mappings
 
     # -- plan -----------------------------------------------------------------------------
     def plan(self, param_groups):
@@ -78,6 +99,8 @@ class Sharder:
             heapq.heappush(heap, (load + cost, r))
         self._owner = owner
         self._order = [p for g in param_groups for p in g["params"]]
+        self._index = {id(p): i for i, p in enumerate(self._order)}
+        self._p2p = None
         return owner
 
     def loads(self, param_groups):
@@ -97,6 +120,10 @@ class Sharder:
     def bind(self, optimizer):
         self._ensure(optimizer)
         self._groups = optimizer.param_groups
+        if self.transport == "p2p" and self._p2p is None:
+            self._p2p = _PeerMaps(self) if _PeerMaps.possible(self) else False
+            if self._p2p is False:
+                self.transport = "nccl"
         self.begin_step()
         return self
 
@@ -108,30 +135,155 @@ class Sharder:
         return lambda shape_idx, i: self._owner[id(stacks[shape_idx][i])] == self.rank
 
     # -- weight sharing ----------------------------------------------------------------------
+    def begin_step(self):
+        self._shared = set()
+        self._pending = []
+        self._point = 0
+
     def share(self, params):
-        """Start broadcasting each of ``params`` that has a gradient from its owner. Every
-        rank must call this with the same tensors in the same order (the optimizers call it
-        once per shape stack / param group, in a fixed order). The broadcasts are enqueued
-        behind the kernels already issued on the current stream and run while later work
-        proceeds; ``sync_params`` waits for them."""
-        if not hasattr(self, "_pending"):
-            self._pending = []
-        for p in params:
-            if p.grad is None or id(p) in self._shared:
-                continue
+        """Start sharing each of ``params`` that has a gradient from its owner. Every rank
+        must call this with the same tensors in the same order (the optimizers call it once
+        per shape stack / param group, in a fixed order); the transfers run behind the
+        kernels already issued on the current stream while later work proceeds, and
+        ``sync_params`` waits for them."""
+        todo = [p for p in params if p.grad is not None and id(p) not in self._shared]
+        for p in todo:
             self._shared.add(id(p))
+        if self.transport == "p2p":
+            self._p2p.share(todo, self._point)
+            self._point += 1
+            return
+        for p in todo:
             src = self._owner[id(p)]
             src_global = dist.get_global_rank(self.group, src) if self.group is not None else src
             self._pending.append(dist.broadcast(p.data, src=src_global, group=self.group, async_op=True))
 
-    def begin_step(self):
-        self._shared = set()
-        self._pending = []
-
     def sync_params(self, optimizer):
         """Share whatever was not shared yet, then make the current stream wait for all of
-        this step's broadcasts."""
+        this step's transfers."""
         self.share(self._order)
+        if self.transport == "p2p":
+            self._p2p.finish()
+            return
         for w in self._pending:
             w.wait()
         self._pending = []
+
+
+class _PeerMaps:
+    """CUDA IPC mappings, side streams and interprocess events of the ``p2p`` transport."""
+
+    @staticmethod
+    def possible(sh):
+        from . import _lib
+        lib = _lib.load()
+        ok = 1
+        for p in sh._order:
+            if sh._owner[id(p)] == sh.rank:
+                h = ctypes.create_string_buffer(64)
+                off = ctypes.c_uint64()
+                if lib.msr_ipc_export(ctypes.c_void_p(p.data_ptr()), h, ctypes.byref(off)) != 0:
+                    ok = 0
+                    break
+        flags = [None] * sh.world
+        dist.all_gather_object(flags, ok, group=sh._host)
+        return all(flags)
+
+    def __init__(self, sh):
+        from . import _lib
+        self.sh = sh
+        self.lib = _lib.load()
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        mine = []
+        for i, p in enumerate(sh._order):
+            if sh._owner[id(p)] == sh.rank:
+                h = ctypes.create_string_buffer(64)
+                off = ctypes.c_uint64()
+                _lib.check(self.lib.msr_ipc_export(ctypes.c_void_p(p.data_ptr()), h, ctypes.byref(off)),
+                           "msr_ipc_export")
+                mine.append((i, bytes(h.raw), off.value))
+        lists = [None] * sh.world
+        dist.all_gather_object(lists, mine, group=sh._host)
+        self.bases = []
+        opened = {}
+        self.remote = {}
+        for r, lst in enumerate(lists):
+            if r == sh.rank:
+                continue
+            for i, h, off in lst:
+                if (r, h) not in opened:
+                    base = ctypes.c_void_p()
+                    _lib.check(self.lib.msr_ipc_import(h, ctypes.byref(base)), "msr_ipc_import")
+                    opened[(r, h)] = base.value
+                    self.bases.append(base.value)
+                self.remote[i] = opened[(r, h)] + off
+        self.streams = {r: torch.cuda.Stream(self.device) for r in range(sh.world) if r != sh.rank}
+        self.owned_events = []
+        self.events = []      # per share point: (local event, {rank: peer event})
+        self.done = self._event_set()
+
+    def _event_set(self):
+        """One interprocess event of this rank plus the opened events of every peer."""
+        from . import _lib
+        ev = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(64)
+        _lib.check(self.lib.msr_ipc_event_create(ctypes.byref(ev), h), "msr_ipc_event_create")
+        self.owned_events.append(ev.value)
+        handles = [None] * self.sh.world
+        dist.all_gather_object(handles, bytes(h.raw), group=self.sh._host)
+        peers = {}
+        for r, hh in enumerate(handles):
+            if r == self.sh.rank:
+                continue
+            pe = ctypes.c_void_p()
+            _lib.check(self.lib.msr_ipc_event_open(hh, ctypes.byref(pe)), "msr_ipc_event_open")
+            self.owned_events.append(pe.value)
+            peers[r] = pe.value
+        return ev.value, peers
+
+    def share(self, params, point):
+        while len(self.events) <= point:
+            self.events.append(self._event_set())
+        ev, peers = self.events[point]
+        main = torch.cuda.current_stream(self.device)
+        self._check(self.lib.msr_event_record(ctypes.c_void_p(ev), ctypes.c_void_p(main.cuda_stream)))
+        dist.barrier(group=self.sh._host)  # every owner's record of this point is enqueued
+        waited = set()
+        for p in params:
+            r = self.sh._owner[id(p)]
+            if r == self.sh.rank:
+                continue
+            s = self.streams[r]
+            if r not in waited:
+                self._check(self.lib.msr_stream_wait_event(ctypes.c_void_p(s.cuda_stream), ctypes.c_void_p(peers[r])))
+                waited.add(r)
+            nbytes = p.numel() * p.element_size()
+            self._check(self.lib.msr_copy_async(ctypes.c_void_p(p.data_ptr()),
+                                                ctypes.c_void_p(self.remote[self.sh._index[id(p)]]), nbytes,
+                                                ctypes.c_void_p(s.cuda_stream)))
+
+    @staticmethod
+    def _check(st):
+        if st:
+            from . import _lib
+            _lib.check(st, "peer copy")
+
+    def finish(self):
+        main = torch.cuda.current_stream(self.device)
+        for s in self.streams.values():
+            main.wait_stream(s)
+        ev, peers = self.done
+        # this rank's copies of its peers' weights are done ...
+        self._check(self.lib.msr_event_record(ctypes.c_void_p(ev), ctypes.c_void_p(main.cuda_stream)))
+        dist.barrier(group=self.sh._host)
+        for e in peers.values():           # ... and no peer still reads this rank's weights
+            self._check(self.lib.msr_stream_wait_event(ctypes.c_void_p(main.cuda_stream), ctypes.c_void_p(e)))
+
+    def __del__(self):
+        try:
+            for e in self.owned_events:
+                self.lib.msr_event_destroy(ctypes.c_void_p(e))
+            for b in self.bases:
+                self.lib.msr_ipc_close(ctypes.c_void_p(b))
+        except Exception:
+            pass
