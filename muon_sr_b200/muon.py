@@ -101,7 +101,13 @@ def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_
     counters stay global, so results do not depend on the number of ranks. ``share(params)``
     is called after each stack so its weights can travel while the next stack computes.
     """
-    for shape_idx, (shape, grp) in enumerate(shape_groups.items()):
+    stacks = list(enumerate(shape_groups.items()))
+    if share is not None:
+        # Largest stacks first, so that the stack whose weights are still in flight when the
+        # step ends is the smallest. Seeds keep each stack's own index, so the bits do not
+        # depend on this order.
+        stacks.sort(key=lambda e: -len(e[1][1]) * K.numel_of(e[1][0]))
+    for shape_idx, (shape, grp) in stacks:
         _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay,
                     step, seeder, owner)
         if share is not None:
