@@ -50,6 +50,11 @@ uint64_t msr_launch_count(void);
  * default). A caller that runs collectives concurrently with the optimizer step (e.g. the
  * sharded step's weight broadcasts) leaves SMs free for them this way. Process-wide. */
 void msr_set_gemm_max_ctas(int max_ctas);
+/* Selects the GEMM kernel of Newton-Schulz and msr_gemm_bf16: `enable` != 0 (the default)
+ * runs 256 x 256 tiles on pairs of SMs (a 2-CTA cluster sharing each B tile), 0 runs
+ * 128 x 256 tiles on single SMs. Both give the same results; process-wide. No counterpart
+ * in the reference (its GEMMs are cuBLAS calls). */
+void msr_set_gemm_pairs(int enable);
 
 /* ---- Philox (test hook) ------------------------------------------------------------
  * out[i] = word 0 of Philox4x32-10 with counter ((ctr_base + i) mod 2^32, 0, 0, 0) and key

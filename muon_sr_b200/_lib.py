@@ -61,6 +61,7 @@ SIGNATURES = [
     ("msr_device_error", c_int, [c_void_p, c_int]),
     ("msr_launch_count", c_uint64, []),
     ("msr_set_gemm_max_ctas", None, [c_int]),
+    ("msr_set_gemm_pairs", None, [c_int]),
     ("msr_philox_fill", c_int, [c_void_p, c_int64, c_uint64, c_uint64, c_void_p]),
     ("msr_grad_accum_bf16", c_int, [c_void_p, c_void_p, c_int64, c_uint64, c_int, c_void_p]),
     ("msr_muon_prepare", c_int, [ctypes.POINTER(PrepareEntry), c_int, c_float, c_float, c_int, c_void_p]),

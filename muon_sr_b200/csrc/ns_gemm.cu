@@ -13,6 +13,9 @@
 // Two 256-column fp32 accumulators (all 512 TMEM columns) let the epilogue of one tile run
 // under the main loop of the next. Operands are either K-major or MN-major (descriptor bit),
 // which covers X X^T, A A and B X for both orientations of X without any transposes.
+// The default variant (gemm_pair_kernel) runs the same roles on clusters of two SMs with
+// tcgen05.mma.cta_group::2 and 256 x 256 tiles, each SM loading half of the B tile; both
+// variants produce identical bits.
 // Every barrier wait has a time limit; on expiry the CTA records an error, drains what it
 // has in flight, frees TMEM and returns.
 #include "common.cuh"
@@ -71,26 +74,29 @@ struct Params {
 
 __device__ __forceinline__ float bf16r(float x) { return bf16_bits_to_f32(rne_bf16_bits(x)); }
 
-// Tile rasterisation: row-blocks (128 rows) are taken in bands of GROUP_M; inside a band
-// the tiles run column by column, rows fastest, so the ~148 tiles of one wave touch about
-// GROUP_M A-panels and 148 / GROUP_M B-panels and both stay in L2.
+// Tile rasterisation: row-blocks are taken in bands of GROUP_M; inside a band the tiles run
+// column by column, rows fastest, so the tiles of one wave touch about GROUP_M A-panels and
+// (wave / GROUP_M) B-panels and both stay in L2. Tiles are TILE_M x BN: 128 x 256 for one
+// CTA, 256 x 256 for a CTA pair; RHO = BN / TILE_M row-blocks span one column-block.
 constexpr int64_t GROUP_M = 8;
 
-// Symmetric mode keeps, in row-block i, the 256-column tiles k >= i/2 (every tile holding
-// an element on or above the diagonal). In a band starting at row-block g0 (even), column
-// k = g0/2 + d holds the band's first min(R, 2d + 2) row-blocks (R = rows in the band).
+// Symmetric mode keeps, in row-block i, the column-blocks k >= i / RHO (every tile holding
+// an element on or above the diagonal). In a band starting at row-block g0 (a multiple of
+// RHO), column k = g0 / RHO + d holds the band's first min(R, RHO (d + 1)) row-blocks.
+template <int RHO>
 __device__ __forceinline__ int64_t sym_band_tiles(int64_t R, int64_t D) {
-  // sum_{d < D} min(R, 2d + 2): the ramp d < R/2 - 1 ... plus full columns
-  const int64_t ramp = R / 2;  // columns with 2d + 2 < R (R even) or <= R (R odd, last band)
-  int64_t s = 0;
+  // sum_{d < D} min(R, RHO (d + 1)): a ramp of dr columns, then full columns of R
+  const int64_t ramp = R / RHO;
   const int64_t dr = D < ramp ? D : ramp;
-  s += dr * (dr + 1);                       // sum of 2d + 2 for d < dr
+  int64_t s = RHO * dr * (dr + 1) / 2;
   if (D > dr) s += (D - dr) * R;
   return s;
 }
 
 // Linear tile index -> (matrix, first row, first column).
+template <int TILE_M>
 __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t& b, int64_t& m0, int64_t& n0) {
+  constexpr int RHO = BN / TILE_M;
   b = t / p.tiles_per_batch;
   int64_t r = t % p.tiles_per_batch;
   if (!p.sym) {
@@ -98,23 +104,23 @@ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t&
     const int64_t g0 = (r / band_tiles) * GROUP_M;
     const int64_t R = min(GROUP_M, p.tiles_m - g0);
     const int64_t w = r % band_tiles;
-    m0 = (g0 + w % R) * BM;
+    m0 = (g0 + w % R) * TILE_M;
     n0 = (w / R) * BN;
     return;
   }
   int64_t g0 = 0;
   for (;;) {
     const int64_t R = min(GROUP_M, p.tiles_m - g0);
-    const int64_t cnt = sym_band_tiles(R, p.tiles_n - g0 / 2);
+    const int64_t cnt = sym_band_tiles<RHO>(R, p.tiles_n - g0 / RHO);
     if (r < cnt) break;
     r -= cnt;
     g0 += GROUP_M;
   }
   const int64_t R = min(GROUP_M, p.tiles_m - g0);
-  // column offset d: prefix over the ramp d*(d+1) (rows 2d+2 each), then R per column
+  // column offset d: the ramp columns hold RHO (d + 1) rows each, later ones R
   int64_t d = 0, rows_d = 0;
   for (;;) {
-    rows_d = min(R, 2 * d + 2);
+    rows_d = min(R, RHO * (d + 1));
     if (r < rows_d) break;
     r -= rows_d;
     ++d;
@@ -124,8 +130,8 @@ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t&
       break;
     }
   }
-  m0 = (g0 + r) * BM;
-  n0 = (g0 / 2 + d) * BN;
+  m0 = (g0 + r) * TILE_M;
+  n0 = (g0 / RHO + d) * BN;
 }
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
@@ -200,6 +206,54 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, i
   }
 }
 
+// One epilogue warp's share of a finished tile: TMEM lane quarter q (rows row0 + 32 q +
+// lane) and column half h of the 256-column accumulator at tmem_acc, with the next chunk's
+// TMEM read and C-operand loads in flight under the current chunk's math.
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int64_t b, int64_t row0, int64_t n0,
+                                              int q, int h, int lane) {
+  constexpr int CHUNKS = BN / 2 / EPI_CW;
+  float alpha = p.alpha, beta = p.beta;
+  if (p.scale != nullptr) {
+    float s = p.scale[b];
+    if (p.scale_is_norm_sq) s = 1.0f / (sqrtf(s) + 1e-7f);
+    if (p.alpha_pow == 1) alpha *= s; else if (p.alpha_pow == 2) alpha *= s * s;
+    if (p.beta_pow == 1) beta *= s;
+  }
+  const int64_t row = row0 + q * 32 + lane;
+  const bool use_c = p.c != nullptr && beta != 0.f;
+  EpiRow er;
+  er.d = p.d + b * p.d_bstride;
+  er.drow = er.d + row * p.ldd;
+  er.crow = use_c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
+  er.row = row;
+  er.ok = row < p.M;
+  const int64_t cbase = n0 + h * (BN / 2);
+  const uint32_t tbase = tmem_acc + static_cast<uint32_t>(h * (BN / 2)) + (static_cast<uint32_t>(q * 32) << 16);
+  uint32_t v[EPI_CW], vn[EPI_CW];
+  U16x8 cv[EPI_G], cvn[EPI_G];
+  __syncwarp();
+  tc::tmem_ld_32x32b_x16(tbase, v);
+  load_c_chunk(p, er, cbase, cv);
+  tc::tmem_ld_wait();
+#pragma unroll
+  for (int cc = 0; cc < CHUNKS; ++cc) {
+    if (cc + 1 < CHUNKS) {
+      __syncwarp();
+      tc::tmem_ld_32x32b_x16(tbase + (cc + 1) * EPI_CW, vn);
+      load_c_chunk(p, er, cbase + (cc + 1) * EPI_CW, cvn);
+    }
+    store_chunk(p, er, cbase + cc * EPI_CW, v, cv, alpha, beta);
+    if (cc + 1 < CHUNKS) {
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < EPI_CW; ++j) v[j] = vn[j];
+#pragma unroll
+      for (int j = 0; j < EPI_G; ++j) cv[j] = cvn[j];
+    }
+  }
+  __syncwarp();
+}
+
 template <int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
@@ -243,7 +297,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int64_t b64, m64, n64;
-        decode_tile(p, t, b64, m64, n64);
+        decode_tile<BM>(p, t, b64, m64, n64);
         const int32_t b = static_cast<int32_t>(b64);
         const int32_t m0 = static_cast<int32_t>(m64);
         const int32_t n0 = static_cast<int32_t>(n64);
@@ -346,7 +400,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // TMEM read and C-operand loads in flight under the current chunk's math.
     const int q = warp & 3;
     const int h = (warp - 4) >> 2;
-    constexpr int CHUNKS = BN / 2 / EPI_CW;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
@@ -356,49 +409,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc::fence_after_sync();
       int64_t b, m0, n0;
-      decode_tile(p, t, b, m0, n0);
-      float alpha = p.alpha, beta = p.beta;
-      if (p.scale != nullptr) {
-        float s = p.scale[b];
-        if (p.scale_is_norm_sq) s = 1.0f / (sqrtf(s) + 1e-7f);
-        if (p.alpha_pow == 1) alpha *= s; else if (p.alpha_pow == 2) alpha *= s * s;
-        if (p.beta_pow == 1) beta *= s;
-      }
-      const int64_t row = m0 + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      const bool use_c = p.c != nullptr && beta != 0.f;
-      EpiRow er;
-      er.d = p.d + b * p.d_bstride;
-      er.drow = er.d + row * p.ldd;
-      er.crow = use_c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
-      er.row = row;
-      er.ok = row_ok;
-      const int64_t cbase = n0 + h * (BN / 2);
-      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN + h * (BN / 2)) +
-                             (static_cast<uint32_t>(q * 32) << 16);
-      uint32_t v[EPI_CW], vn[EPI_CW];
-      U16x8 cv[EPI_G], cvn[EPI_G];
-      __syncwarp();
-      tc::tmem_ld_32x32b_x16(tbase, v);
-      load_c_chunk(p, er, cbase, cv);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int cc = 0; cc < CHUNKS; ++cc) {
-        if (cc + 1 < CHUNKS) {
-          __syncwarp();
-          tc::tmem_ld_32x32b_x16(tbase + (cc + 1) * EPI_CW, vn);
-          load_c_chunk(p, er, cbase + (cc + 1) * EPI_CW, cvn);
-        }
-        store_chunk(p, er, cbase + cc * EPI_CW, v, cv, alpha, beta);
-        if (cc + 1 < CHUNKS) {
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < EPI_CW; ++j) v[j] = vn[j];
-#pragma unroll
-          for (int j = 0; j < EPI_G; ++j) cv[j] = cvn[j];
-        }
-      }
-      __syncwarp();
+      decode_tile<BM>(p, t, b, m0, n0);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane);
       tc::fence_before_sync();
       tc::mbar_arrive(&S.tmem_empty[acc]);
       if (++acc == 2) {
@@ -412,6 +424,233 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2, issued by the even CTA of the pair. Each CTA loads its own 128
+// rows of A and its own 128 rows of B (half of the tile's output columns) and receives its
+// 128 rows of the accumulator in its TMEM, so a pair moves 64 KB per 64-deep k-block where
+// two single CTAs move 96 KB for the same MMA work: a third less L2 -> shared-memory
+// traffic, and a 6-stage ring in the same shared memory.
+//
+// Barriers: `full` of the leader counts both CTAs' copies of a stage (the leader expects the
+// pair's bytes; each CTA's copies complete on it); the MMA commit arrives on `empty` and
+// `tmem_full` of both CTAs; both CTAs' epilogue warps arrive on the leader's `tmem_empty`.
+// A wait that gives up stops its own CTA and sets the peer's abort flag; copies already in
+// flight get a bounded settling time, and a cluster barrier keeps both CTAs resident until
+// neither touches the other's shared memory.
+// ---------------------------------------------------------------------------------------
+namespace pair {
+constexpr int TILE_M = 256;
+constexpr int HALF = 128;
+constexpr int STAGES = 6;
+constexpr int A_BYTES = HALF * BK * 2;
+constexpr int B_BYTES = HALF * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t EMPTY_ARRIVALS = 2 * (EPI_THREADS / 32);  // one per epilogue warp of each CTA
+constexpr uint64_t SETTLE_NS = 200000;  // after giving up: time for copies in flight to land
+constexpr uint16_t BOTH = 0x3;
+
+struct SharedStorage {
+  alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+}  // namespace pair
+
+// Sleeps for about `ns` nanoseconds of wall time.
+__device__ __forceinline__ void settle(uint64_t ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  do {
+    __nanosleep(1000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < ns);
+}
+
+template <int A_MN, int B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  using pair::HALF;
+  using pair::STAGES;
+  using pair::TILE_M;
+  extern __shared__ uint8_t smem_raw[];
+  pair::SharedStorage& S =
+      *reinterpret_cast<pair::SharedStorage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();  // 0: the leader, which issues the MMAs
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t num_pairs = gridDim.x >> 1;
+  volatile int* abort = &S.abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&S.full[s], 1);
+      tc::mbar_init(&S.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&S.tmem_full[a], 1);
+      tc::mbar_init(&S.tmem_empty[a], pair::EMPTY_ARRIVALS);
+    }
+    tc::mbar_init(&S.drain, 1);
+    S.abort = 0;
+    tc::fence_mbar_init();
+    tc::tma_prefetch_desc(&tmA);
+    tc::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(&S.tmem_base, TMEM_COLS);
+    tc::tmem_relinquish_pair();
+    tc::fence_before_sync();
+  }
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy
+  tc::fence_after_sync();
+  const uint32_t tmem_base = S.tmem_base;
+  const int64_t num_kb = (p.K + BK - 1) / BK;
+  const uint32_t peer_abort = tc::cluster_addr(&S.abort, rank ^ 1u);
+  auto give_up = [&](int code) {
+    record_error(code);
+    *abort = 1;
+    tc::st_cluster_u32(peer_abort, 1u);
+  };
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer (both CTAs) ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = pair_id; t < p.num_tiles && ok; t += num_pairs) {
+        int64_t b64, m64, n64;
+        decode_tile<TILE_M>(p, t, b64, m64, n64);
+        const int32_t b = static_cast<int32_t>(b64);
+        const int32_t ma = static_cast<int32_t>(m64 + HALF * rank);
+        const int32_t nb = static_cast<int32_t>(n64 + HALF * rank);
+        for (int64_t kb = 0; kb < num_kb; ++kb) {
+          if (!tc::mbar_wait(&S.empty[stage], phase ^ 1u, abort, WAIT_LIMIT_NS)) {
+            give_up(ERR_TMA_WAIT);
+            ok = false;
+            break;
+          }
+          uint8_t* sa = S.stage[stage];
+          uint8_t* sb = S.stage[stage] + pair::A_BYTES;
+          const int32_t k0 = static_cast<int32_t>(kb * BK);
+          if (rank == 0) tc::mbar_arrive_expect_tx(&S.full[stage], 2 * pair::STAGE_BYTES);
+          const uint32_t bar = tc::cluster_addr(&S.full[stage], 0);
+          if (A_MN) {
+            tc::tma_load_3d_pair(sa, &tmA, bar, ma, k0, b);
+            tc::tma_load_3d_pair(sa + 8192, &tmA, bar, ma + 64, k0, b);
+          } else {
+            tc::tma_load_3d_pair(sa, &tmA, bar, k0, ma, b);
+          }
+          if (B_MN) {
+            tc::tma_load_3d_pair(sb, &tmB, bar, nb, k0, b);
+            tc::tma_load_3d_pair(sb + 8192, &tmB, bar, nb + 64, k0, b);
+          } else {
+            tc::tma_load_3d_pair(sb, &tmB, bar, k0, nb, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) settle(pair::SETTLE_NS);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (leader only) ------------------------------
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(TILE_M, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
+      for (int64_t t = pair_id; t < p.num_tiles && ok; t += num_pairs) {
+        if (!tc::mbar_wait(&S.tmem_empty[acc], acc_phase ^ 1u, abort, WAIT_LIMIT_NS)) {
+          give_up(ERR_MMA_WAIT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int64_t kb = 0; kb < num_kb; ++kb) {
+          if (!tc::mbar_wait(&S.full[stage], phase, abort, WAIT_LIMIT_NS)) {
+            give_up(ERR_MMA_WAIT);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t sa = tc::smem_addr(S.stage[stage]);
+          const uint32_t sb = sa + pair::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint32_t aoff = A_MN ? static_cast<uint32_t>(k * UMMA_K * 128) : static_cast<uint32_t>(k * UMMA_K * 2);
+            const uint32_t boff = B_MN ? static_cast<uint32_t>(k * UMMA_K * 128) : static_cast<uint32_t>(k * UMMA_K * 2);
+            const uint64_t adesc = tc::smem_desc_sw128(sa + aoff, a_lbo, 1024u);
+            const uint64_t bdesc = tc::smem_desc_sw128(sb + boff, b_lbo, 1024u);
+            tc::mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit_pair(&S.empty[stage], pair::BOTH);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc::mma_commit_pair(&S.tmem_full[acc], pair::BOTH);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued above (they read both CTAs' shared memory) has finished before
+      // either CTA may leave.
+      tc::mma_commit_pair(&S.drain, 0x1);
+      volatile int no_abort = 0;
+      tc::mbar_wait(&S.drain, 0, &no_abort, WAIT_LIMIT_NS);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------ epilogue (both CTAs) ------------------------------
+    const int q = warp & 3;
+    const int h = (warp - 4) >> 2;
+    const uint32_t leader_empty[2] = {tc::cluster_addr(&S.tmem_empty[0], 0), tc::cluster_addr(&S.tmem_empty[1], 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = pair_id; t < p.num_tiles; t += num_pairs) {
+      if (!tc::mbar_wait(&S.tmem_full[acc], acc_phase, abort, WAIT_LIMIT_NS)) {
+        give_up(ERR_EPI_WAIT);
+        break;
+      }
+      tc::fence_after_sync();
+      int64_t b, m0, n0;
+      decode_tile<TILE_M>(p, t, b, m0, n0);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane);
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(leader_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  tc::cluster_sync();  // neither CTA touches the other's shared memory or TMEM any more
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -471,6 +710,54 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaSt
   return check_launch("gemm_kernel");
 }
 
+size_t pair_smem_bytes() { return sizeof(pair::SharedStorage) + 1024; }
+
+std::atomic<int> g_gemm_pairs{1};
+
+// Clusters of two that fit on the device at once (a GPC with an odd number of free SMs
+// leaves one idle), per kernel variant and device.
+constexpr int MAX_DEVICES = 64;
+std::atomic<int> g_pair_capacity[4][MAX_DEVICES];
+
+template <int A_MN, int B_MN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+  const int smem = static_cast<int>(pair_smem_bytes());
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>& cap_slot = g_pair_capacity[A_MN * 2 + B_MN][dev % MAX_DEVICES];
+  int pairs = cap_slot.load(std::memory_order_relaxed);
+  if (pairs <= 0) {
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0)
+      return fail(MSR_ERR_CUDA, "cudaOccupancyMaxActiveClusters: %s (%d)", cudaGetErrorString(e), n);
+    pairs = n;
+    cap_slot.store(n, std::memory_order_relaxed);
+  }
+  const int cap = g_gemm_max_ctas.load(std::memory_order_relaxed);
+  if (cap > 0) pairs = std::min(pairs, std::max(1, cap / 2));
+  pairs = static_cast<int>(std::min<int64_t>(p.num_tiles, pairs));
+  cfg.gridDim = dim3(2 * pairs);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "gemm_pair_kernel launch: %s", cudaGetErrorString(e));
+  return check_launch("gemm_pair_kernel");
+}
+
 // D[b] = alpha_b * op(A)[b] x op(B)[b]^T + beta_b * C[b]. A K-major: [batch][M][K]; MN-major:
 // [batch][K][M]. B K-major: [batch][N][K]; MN-major: [batch][K][N]. C, D: [batch][M][N] with
 // row strides ldc, ldd.
@@ -479,21 +766,26 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
          int64_t K, float alpha, float beta, const float* scale, int alpha_pow, int beta_pow, int scale_is_norm_sq,
          int ref_round, int sym, cudaStream_t s) {
   if (sym && M != N) return fail(MSR_ERR_INVALID, "symmetric GEMM needs M == N");
+  const bool pairs = g_gemm_pairs.load(std::memory_order_relaxed) != 0;
+  const int64_t tile_m = pairs ? pair::TILE_M : BM;
+  // K-major boxes: one CTA's rows of A (128) and of B (256 alone, 128 as half of a pair)
+  const uint32_t b_rows = pairs ? pair::HALF : BN;
   CUtensorMap ta, tb;
   int st = a_mn ? make_map(&ta, a, M, K, batch, a_bstride, 64) : make_map(&ta, a, K, M, batch, a_bstride, BM);
   if (st) return st;
-  st = b_mn ? make_map(&tb, b, N, K, batch, b_bstride, 64) : make_map(&tb, b, K, N, batch, b_bstride, BN);
+  st = b_mn ? make_map(&tb, b, N, K, batch, b_bstride, 64) : make_map(&tb, b, K, N, batch, b_bstride, b_rows);
   if (st) return st;
   Params p{};
   p.M = M; p.N = N; p.K = K; p.batch = batch;
-  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_m = (M + tile_m - 1) / tile_m;
   p.tiles_n = (N + BN - 1) / BN;
   p.sym = sym;
   p.tiles_per_batch = p.tiles_m * p.tiles_n;
   if (sym) {
-    // row-block i keeps tiles i/2 .. tiles_n-1 (see decode_tile)
+    // row-block i keeps column-blocks i / RHO .. tiles_n - 1 (see decode_tile)
+    const int64_t rho = BN / tile_m;
     p.tiles_per_batch = 0;
-    for (int64_t i = 0; i < p.tiles_m; ++i) p.tiles_per_batch += p.tiles_n - i / 2;
+    for (int64_t i = 0; i < p.tiles_m; ++i) p.tiles_per_batch += p.tiles_n - i / rho;
   }
   p.num_tiles = p.tiles_per_batch * batch;
   p.d = static_cast<uint16_t*>(d);
@@ -502,6 +794,12 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
   p.alpha = alpha; p.beta = beta;
   p.scale = scale; p.alpha_pow = alpha_pow; p.beta_pow = beta_pow; p.scale_is_norm_sq = scale_is_norm_sq;
   p.ref_round = ref_round;
+  if (pairs) {
+    if (a_mn && b_mn) return launch_pair<1, 1>(ta, tb, p, s);
+    if (a_mn) return launch_pair<1, 0>(ta, tb, p, s);
+    if (b_mn) return launch_pair<0, 1>(ta, tb, p, s);
+    return launch_pair<0, 0>(ta, tb, p, s);
+  }
   if (a_mn && b_mn) return launch<1, 1>(ta, tb, p, s);
   if (a_mn) return launch<1, 0>(ta, tb, p, s);
   if (b_mn) return launch<0, 1>(ta, tb, p, s);
@@ -663,6 +961,8 @@ using namespace msr::gemm;
 extern "C" {
 
 void msr_set_gemm_max_ctas(int max_ctas) { g_gemm_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
+
+void msr_set_gemm_pairs(int enable) { g_gemm_pairs.store(enable ? 1 : 0); }
 
 int msr_device_error(msr_stream_t stream, int clear) {
   cudaError_t e = cudaStreamSynchronize(to_stream(stream));

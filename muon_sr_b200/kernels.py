@@ -222,6 +222,12 @@ def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=N
     return d
 
 
+def set_gemm_pairs(enable: bool) -> None:
+    """Run the Newton-Schulz GEMMs on SM pairs (256 x 256 tiles, the default) or on single
+    SMs (128 x 256 tiles). Both produce the same bits; process-wide."""
+    _lib.load().msr_set_gemm_pairs(1 if enable else 0)
+
+
 def device_error(clear: bool = True, device=None) -> int:
     """Synchronise the current stream and return (and clear) the library's device error code."""
     return int(_lib.load().msr_device_error(stream_handle(device), int(clear)))

@@ -84,6 +84,45 @@ def test_gemm_symmetric_mode_equals_full(shape, a_mn):
     assert torch.equal(bf.view(torch.int16), bs.view(torch.int16))
 
 
+@pytest.mark.parametrize("shape", [(2, 512, 768, 320), (1, 296, 520, 200), (3, 136, 64, 72), (1, 24, 40, 16)])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_pairs_equal_single_ctas(shape, a_mn, b_mn):
+    """256 x 256 tiles on SM pairs (cta_group::2) and 128 x 256 tiles on single SMs give the
+    same bits: plain and fused epilogues, symmetric mode, ragged edges."""
+    batch, M, N, Kd = shape
+    g = torch.Generator(device=DEV).manual_seed(M + N + Kd + 2 * a_mn + b_mn)
+    a = torch.randn(batch, *((Kd, M) if a_mn else (M, Kd)), device=DEV, generator=g).bfloat16()
+    b = torch.randn(batch, *((Kd, N) if b_mn else (N, Kd)), device=DEV, generator=g).bfloat16()
+    c = torch.randn(batch, M, N, device=DEV, generator=g).bfloat16()
+    x = torch.randn(batch, *((Kd, M) if a_mn else (M, Kd)), device=DEV, generator=g).bfloat16()
+    outs = []
+    try:
+        for pairs in (True, False):
+            K.set_gemm_pairs(pairs)
+            outs.append([K.gemm_bf16(a, a_mn, b, b_mn),
+                         K.gemm_bf16(a, a_mn, b, b_mn, c, 2.0315, -4.775, ref_rounding=True),
+                         K.gemm_bf16(x, a_mn, x, a_mn, ref_rounding=True, symmetric=True)])
+            assert K.device_error() == 0
+    finally:
+        K.set_gemm_pairs(True)
+    for p, s in zip(*outs):
+        assert torch.equal(p.view(torch.int16), s.view(torch.int16))
+
+
+@pytest.mark.parametrize("shape", [(16, 512, 512), (3, 1024, 256), (2, 768, 3072), (2, 104, 72)])
+def test_ns_pairs_equal_single_ctas(shape):
+    g = torch.Generator(device=DEV).manual_seed(sum(shape))
+    x = (torch.randn(*shape, device=DEV, generator=g) * 1e-3).bfloat16()
+    outs = []
+    try:
+        for pairs in (True, False):
+            K.set_gemm_pairs(pairs)
+            outs.append(K.newton_schulz(x, 5))
+    finally:
+        K.set_gemm_pairs(True)
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+
+
 def test_ns_matches_reference_golden():
     """Against the reference's own outputs, computed on the CPU. The quintic iteration
     amplifies last-bit differences of the fp32 GEMM accumulation (CPU vs tensor cores) to
