@@ -195,6 +195,8 @@ def run_ours(args, rank, world, local_rank):
     timers = Timers()
     for name in ("newton_schulz", "muon_prepare", "muon_apply", "adamw_sr"):
         timers.wrap(K, name)
+    if shard is not None:
+        timers.wrap(Sharder, "sync_params")  # end of step: waits for the weight exchange
     # the optimizer module imported the wrappers by module reference (K.<name>), so the
     # wrapped functions are the ones it calls
 
@@ -228,6 +230,10 @@ def run_ours(args, rank, world, local_rank):
     n_muon = sum(p.numel() for p in muon)
     n_adam = sum(p.numel() for p in adam)
     breakdown = {k: v / args.steps for k, v in tot.items()}
+    per_rank = [breakdown]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, breakdown)
 
     # ---- 8-bit blockwise AdamW on the same tensors ----
     params = muon + adam
@@ -290,6 +296,7 @@ def run_ours(args, rank, world, local_rank):
             "ns_tflops": ns_tflops, "ns_tflop_per_step": total_flops / 1e12,
             "adamw8bit_hbm_gbs": a8_gbs, "adamw8bit_step_ms": a8_step_ms, "adamw8bit_kernel_ms": a8_kernel_ms,
             "breakdown_ms_per_step": breakdown,
+            "breakdown_ms_per_step_per_rank": per_rank if world > 1 else None,
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (Newton-Schulz chain)",
                          "achieved": ns_tflops, "peak": peak_ns, "unit": "TFLOP/s",
                          "frac": (ns_tflops / peak_ns) if ns_tflops else None,

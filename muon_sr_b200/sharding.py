@@ -14,7 +14,10 @@ NCCL (NVLink / NVSwitch), so the step's work is divided by the number of ranks.
   broadcast from their owners on NCCL's stream, so the transfers run under the next
   stacks' Newton-Schulz work; the step ends by waiting for all of them.
 * Optimizer state (momentum, moments) stays with the owner; ``state_dict()`` on a rank holds
-  valid values only for the parameters that rank owns.
+  valid values only for the parameters that rank owns until ``gather_state`` copies the
+  owners' values over (for checkpoints).
+* ``reduce_grads`` replaces the data-parallel all-reduce of the gradients: each gradient
+  only has to reach its owner.
 """
 import ctypes
 import heapq
@@ -168,6 +171,77 @@ class Sharder:
         for w in self._pending:
             w.wait()
         self._pending = []
+
+    # -- gradients -----------------------------------------------------------------------
+    def _src(self, r):
+        return dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    def reduce_grads(self, optimizer, average: bool = True):
+        """Collective replacing the data-parallel gradient all-reduce: every parameter's
+        gradient is summed (or averaged) over the ranks onto its owner only, one bucket per
+        owner, which moves half the bytes of an all-reduce. Non-owners keep their local
+        gradients (the step skips their parameters but still sees that they have one).
+        Every rank calls it after backward with the same parameters holding gradients."""
+        self._ensure(optimizer)
+        for r in range(self.world):
+            grads = [p.grad for p in self._order if p.grad is not None and self._owner[id(p)] == r]
+            if not grads:
+                continue
+            flat = torch.cat([g.reshape(-1) for g in grads])
+            op = dist.ReduceOp.SUM
+            if average and dist.get_backend(self.group) == "nccl":
+                op = dist.ReduceOp.AVG
+            dist.reduce(flat, dst=self._src(r), op=op, group=self.group)
+            if r != self.rank:
+                continue
+            if average and op == dist.ReduceOp.SUM:
+                flat.div_(self.world)
+            off = 0
+            for g in grads:
+                n = g.numel()
+                g.copy_(flat[off:off + n].view_as(g))
+                off += n
+
+    # -- checkpoints -----------------------------------------------------------------------
+    def gather_state(self, optimizer, dst=None):
+        """Collective: copy every parameter's optimizer state from its owner to rank ``dst``
+        (every rank when None), so that ``optimizer.state_dict()`` there holds the whole
+        state with the reference's keys and dtypes (checkpoints stay interchangeable with
+        the single-GPU classes). Loading needs no counterpart: every rank loads the full
+        checkpoint and uses the part it owns."""
+        self._ensure(optimizer)
+        order = [p for g in optimizer.param_groups for p in g["params"]]
+        meta = {}
+        for i, p in enumerate(order):
+            if self._owner[id(p)] != self.rank:
+                continue
+            meta[i] = {k: (("t", tuple(v.shape), str(v.dtype).split(".")[-1]) if torch.is_tensor(v) else ("v", v))
+                       for k, v in optimizer.state.get(p, {}).items()}
+        metas = [None] * self.world
+        dist.all_gather_object(metas, meta, group=self.group)
+        for i, p in enumerate(order):
+            owner = self._owner[id(p)]
+            spec = metas[owner].get(i)
+            if not spec:
+                continue
+            keep = owner != self.rank and (dst is None or dst == self.rank)
+            st = optimizer.state[p]
+            for k in sorted(spec):
+                kind = spec[k][0]
+                if kind == "v":
+                    if keep:
+                        st[k] = spec[k][1]
+                    continue
+                shape, dtype = spec[k][1], getattr(torch, spec[k][2])
+                t = st.get(k) if torch.is_tensor(st.get(k)) else None
+                if owner != self.rank and (t is None or tuple(t.shape) != shape or t.dtype != dtype):
+                    t = torch.empty(shape, dtype=dtype, device=p.device)
+                buf = t if t.is_contiguous() else t.contiguous()
+                dist.broadcast(buf, src=self._src(owner), group=self.group)
+                if keep:
+                    if buf is not t:
+                        t.copy_(buf)
+                    st[k] = t
 
 
 class _PeerMaps:

@@ -129,3 +129,81 @@ def test_sharding_plan_two_ranks_gloo():
     assert set(gathered[0]) == {0, 1}
     assert max(loads) / min(loads) < 1.25, loads
     assert ok
+
+
+def _state_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mk = lambda *s: torch.nn.Parameter(torch.zeros(*s, dtype=torch.bfloat16))
+        muon = [mk(8, 16), mk(8, 16), mk(16, 8), mk(8, 16), mk(4, 4)]
+        adam = [mk(16), mk(5, 3), mk(7)]
+        opt = TritonMuonSRWithAuxAdam([dict(params=muon, use_muon=True), dict(params=adam, use_muon=False)],
+                                      batch_ns=True)
+        sh = Sharder()
+        sh.plan(opt.param_groups)
+        order = [p for g in opt.param_groups for p in g["params"]]
+        owner = [sh._owner[id(p)] for p in order]
+        val = lambda i: float(2 * (i % 16) + owner[i])
+
+        def fill():
+            # what a sharded step leaves behind: every rank has every key, owners hold values
+            for i, p in enumerate(order):
+                mine = owner[i] == rank
+                st = opt.state[p]
+                st["step"] = 3 if mine else 0
+                if i < len(muon):
+                    st["momentum_buffer"] = torch.full(p.shape, val(i) if mine else -1.0, dtype=torch.bfloat16)
+                else:
+                    st["ema"] = torch.full(p.shape, val(i) if mine else -1.0, dtype=torch.bfloat16)
+                    st["ema_squared"] = torch.full(p.shape, val(i) + 0.5 if mine else -1.0, dtype=torch.bfloat16)
+
+        def complete():
+            ok = True
+            for i, p in enumerate(order):
+                st = opt.state[p]
+                ok &= st["step"] == 3
+                if i < len(muon):
+                    ok &= bool((st["momentum_buffer"].float() == val(i)).all())
+                else:
+                    ok &= bool((st["ema"].float() == val(i)).all()) and bool((st["ema_squared"].float() == val(i) + 0.5).all())
+            return ok
+
+        fill()
+        sh.gather_state(opt)
+        ok_all = complete()
+        sd = opt.state_dict()
+        keys = [sorted(sd["state"][i].keys()) for i in range(len(order))]
+        fill()
+        sh.gather_state(opt, dst=0)
+        ok_dst = complete() if rank == 0 else not complete()
+
+        for i, p in enumerate(order):
+            p.grad = torch.full(p.shape, float(rank + 1 + i % 7), dtype=torch.bfloat16)
+        sh.reduce_grads(opt)
+        ok_red = all(bool((p.grad.float() == ((i % 7) + 1.5 if owner[i] == rank else rank + 1 + i % 7)).all())
+                     for i, p in enumerate(order))
+        out.put((rank, ok_all, ok_dst, ok_red, keys, sorted(set(owner))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_state_gather_and_grad_reduce_two_ranks_gloo():
+    """Sharder.gather_state completes every rank's (or one rank's) optimizer state from the
+    owners, state_dict() keeps the reference's keys; reduce_grads averages each gradient
+    onto its owner and leaves the others' local gradients alone."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 1000
+    procs = [ctx.Process(target=_state_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120), q.get(timeout=120)])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok_all, ok_dst, ok_red, keys, owners in res:
+        assert owners == [0, 1]
+        assert ok_all and ok_dst and ok_red, (rank, ok_all, ok_dst, ok_red)
+        assert keys[:5] == [["momentum_buffer", "step"]] * 5
+        assert keys[5:] == [["ema", "ema_squared", "step"]] * 3

@@ -1,9 +1,11 @@
-"""Sharded optimizer steps on 2 GPUs (NCCL) produce exactly the single-GPU bits.
+"""Sharded optimizer steps on 2 GPUs produce exactly the single-GPU bits.
 
-Each rank updates only the tensors the Sharder assigns to it and receives the others by
-broadcast; seeds and Philox counters are global and Newton-Schulz computes each matrix on
-its own, so the parameters after every step must equal a 1-GPU run bit for bit. Skipped on
-a box with fewer than 2 GPUs.
+Each rank updates only the tensors the Sharder assigns to it and receives the others over
+NVLink; seeds and Philox counters are global and Newton-Schulz computes each matrix on its
+own, so the parameters after every step must equal a 1-GPU run bit for bit. The gradients
+start rank-local and reach their owners through ``reduce_grads``; after the steps
+``gather_state`` must reproduce the single-GPU optimizer state (checkpoint interop).
+Skipped on a box with fewer than 2 GPUs.
 """
 import os
 
@@ -28,24 +30,51 @@ def _grads(step, device):
     return [(torch.randn(*s, generator=g) * 1e-3).bfloat16().to(device) for s in SHAPES_MUON + SHAPES_ADAM]
 
 
-def _run(device, shard, steps=3, batch_ns=True):
+def _state_tensors(opt):
+    """Every tensor of state_dict()["state"], in a fixed order."""
+    sd = opt.state_dict()["state"]
+    return [sd[i][k] for i in sorted(sd) for k in sorted(sd[i]) if torch.is_tensor(sd[i][k])]
+
+
+def _run(device, shard, steps=3, batch_ns=True, rank=0):
+    """Hybrid steps then 8-bit steps. With ``shard``: each rank starts from local gradients
+    (2 g on rank 0, 0 elsewhere) that ``reduce_grads`` averages onto the owners, and the
+    state is gathered from the owners before it is returned."""
     from muon_sr_b200 import TritonAdamW8bit, TritonMuonSRWithAuxAdam
     muon, adam = _params(device)
+    sh = shard() if shard else None
     opt = TritonMuonSRWithAuxAdam([dict(params=muon, use_muon=True, weight_decay=0.01),
                                    dict(params=adam, use_muon=False, weight_decay=0.01)],
-                                  batch_ns=batch_ns, shard=shard() if shard else None)
+                                  batch_ns=batch_ns, shard=sh)
+
+    def set_grads(params, grads):
+        for p, g in zip(params, grads):
+            p.grad = g if sh is None else (g * 2 if rank == 0 else torch.zeros_like(g))
+
     for k in range(steps):
-        for p, g in zip(muon + adam, _grads(k, device)):
-            p.grad = g
+        set_grads(muon + adam, _grads(k, device))
+        if sh is not None:
+            sh.reduce_grads(opt)
         opt.step()
     params8 = [torch.nn.Parameter(p.detach().clone()) for p in muon + adam]
-    opt8 = TritonAdamW8bit(params8, lr=1e-3, weight_decay=0.01, shard=shard() if shard else None)
+    sh8 = shard() if shard else None
+    opt8 = TritonAdamW8bit(params8, lr=1e-3, weight_decay=0.01, shard=sh8)
     for k in range(2):
-        for p, g in zip(params8, _grads(10 + k, device)):
-            p.grad = g
+        set_grads(params8, _grads(10 + k, device))
+        if sh8 is not None:
+            sh8.reduce_grads(opt8)
         opt8.step()
+    if sh is not None:
+        sh.gather_state(opt)
+        sh8.gather_state(opt8)
     torch.cuda.synchronize()
-    return [p.detach().cpu() for p in muon + adam + params8]
+    state = _state_tensors(opt) + _state_tensors(opt8)
+    return [p.detach().cpu() for p in muon + adam + params8] + [t.detach().cpu() for t in state]
+
+
+def _bits(t):
+    """Raw bytes of a tensor of any dtype (bf16 weights/moments, uint8 codes, fp32 absmax)."""
+    return t.contiguous().view(-1).view(torch.uint8).numpy()
 
 
 def _worker(rank, world, port, q):
@@ -55,9 +84,9 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        out = _run(torch.device("cuda", rank), Sharder)
+        out = _run(torch.device("cuda", rank), Sharder, rank=rank)
         if rank == 0:
-            q.put([t.view(torch.int16).numpy() for t in out])
+            q.put([_bits(t) for t in out])
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -66,7 +95,7 @@ def _worker(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_sharded_step_equals_single_gpu():
     import numpy as np
-    single = [t.view(torch.int16).numpy() for t in _run(torch.device("cuda", 0), None)]
+    single = [_bits(t) for t in _run(torch.device("cuda", 0), None)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29700 + os.getpid() % 500
@@ -78,4 +107,4 @@ def test_two_gpu_sharded_step_equals_single_gpu():
         p.join(timeout=120)
         assert p.exitcode == 0
     for i, (a, b) in enumerate(zip(single, sharded)):
-        assert np.array_equal(a, b), f"tensor {i} differs between 1 and 2 GPUs"
+        assert np.array_equal(a, b), f"tensor {i} (parameters, then optimizer state) differs between 1 and 2 GPUs"
