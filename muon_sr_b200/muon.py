@@ -8,8 +8,8 @@ keys and seed formulas (muon_sr/triton_muon_sr.py:180-373, muon_sr/muon_sr.py:23
   on the same CUDA kernels with seeds drawn from torch's default generator (the reference
   draws its rounding noise with ``torch.randint_like``), and keep those classes' state keys.
 
-Every step is: a multi-tensor prepare kernel (momentum, Nesterov, SR momentum, RNE update,
-per-matrix squared Frobenius norm), the tcgen05 Newton-Schulz chain over each shape stack,
+Every step is: a multi-tensor prepare kernel (momentum, Nesterov, SR momentum, RNE update),
+the tcgen05 Newton-Schulz chain over each shape stack,
 and a multi-tensor apply kernel (decay, scaled update, SR weights). ``shard`` (optional)
 spreads the matrices over the ranks of a process group (see ``sharding``).
 """
@@ -78,6 +78,11 @@ class _Seeder:
             return int(torch.randint(0, 1 << 32, (1,), dtype=torch.int64).item())
         return deterministic_seed(step, idx, salt)
 
+    def skip(self, step, idx, salt):
+        """Consume the seed of a tensor another rank updates, so that every rank draws the
+        same sequence from torch's generator as a single-GPU run."""
+        self(step, idx, salt)
+
 
 def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, step, param_idx, seeder):
     """Per-parameter Muon step (``_triton_muon_step``, triton_muon_sr.py:116-120)."""
@@ -90,7 +95,7 @@ def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, s
 
 
 def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
-                    seeder, owner=None, share=None):
+                    seeder, owner=None, share=None, segments=None):
     """Batched step over shape stacks (``_triton_muon_batch_step``, triton_muon_sr.py:128-177).
 
     Prepare runs once per stack with seed S(step, shape_idx, 0) and counters running over the
@@ -99,24 +104,37 @@ def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_
     falls back to per-parameter steps with param_idx = shape_idx * 10000 + i.
     ``owner(shape_idx, i) -> bool`` restricts the work to this rank's matrices; seeds and
     counters stay global, so results do not depend on the number of ranks. ``share(params)``
-    is called after each stack so its weights can travel while the next stack computes.
+    is called after each stack (and, with ``segments``, after each segment of a stack) so its
+    weights can travel while the rest computes.
     """
     stacks = list(enumerate(shape_groups.items()))
-    if share is not None:
+    if share is not None and not seeder.random:
         # Largest stacks first, so that the stack whose weights are still in flight when the
         # step ends is the smallest. Seeds keep each stack's own index, so the bits do not
-        # depend on this order.
+        # depend on this order (seeds drawn from torch's generator do: those keep the order).
         stacks.sort(key=lambda e: -len(e[1][1]) * K.numel_of(e[1][0]))
     for shape_idx, (shape, grp) in stacks:
         _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay,
-                    step, seeder, owner)
+                    step, seeder, owner, share, segments)
         if share is not None:
             share(grp)
 
 
+def _segments(n, count):
+    """Split range(n) into ``count`` consecutive index ranges of near-equal length."""
+    count = max(1, min(n, count))
+    bounds = [n * s // count for s in range(count + 1)]
+    return [range(bounds[s], bounds[s + 1]) for s in range(count)]
+
+
 def _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
-                seeder, owner):
-    """One shape stack of ``muon_batch_step``."""
+                seeder, owner, share=None, segments=None):
+    """One shape stack of ``muon_batch_step``. With ``segments(shape, n) -> count`` the
+    stack's global index range is cut into that many consecutive segments; each rank runs
+    its own matrices segment by segment and ``share`` is called after every segment (on
+    every rank, also when it owned none of it), so the weights start travelling while the
+    rest of the stack computes. Chunks never span segments; the bits are those of the
+    unsegmented step."""
     active = [p for p in grp if p.grad is not None]
     if not active:
         return
@@ -127,24 +145,39 @@ def _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov
             if owner is None or owner(shape_idx, i):
                 muon_single_step(p, _grad_of(p), stacked_buf[i], beta, nesterov, ns_steps, lr, weight_decay,
                                  step, shape_idx * 10000 + i, seeder)
+            else:
+                seeder.skip(step, shape_idx * 10000 + i, 0)
+                seeder.skip(step, shape_idx * 10000 + i, 1)
         return
     mine = [i for i in range(len(grp)) if owner is None or owner(shape_idx, i)]
-    if not mine:
-        return
+    segs = _segments(len(grp), segments(shape, len(grp)) if (segments and share) else 1)
     if len(shape) < 2:
         raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
     numel = K.numel_of(shape)
-    work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=stacked_buf.device)
+    work = None
+    # seeds in the single-GPU draw order: the stack's prepare seed, then one apply seed per
+    # matrix in index order (all of them on every rank)
     prep_seed = seeder(step, shape_idx, 0)
-    K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
-                    for j, i in enumerate(mine)], beta, nesterov)
+    apply_seeds = [seeder(step, shape_idx * 10000 + i, 1) for i in range(len(grp))]
+    if mine:
+        work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=stacked_buf.device)
+        K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
+                        for j, i in enumerate(mine)], beta, nesterov)
     k = max(1, NS_CHUNK_NUMEL // max(1, numel))
     scale = K.ns_scale(shape)
-    for s in range(0, len(mine), k):
-        out = K.newton_schulz(work[s:s + k], ns_steps)
-        K.muon_apply([(grp[mine[s + j]], out[j], scale, seeder(step, shape_idx * 10000 + mine[s + j], 1))
-                      for j in range(out.shape[0])], lr, weight_decay)
-        del out
+    pos = 0  # position in `mine` (and `work`) where the current segment starts
+    for seg in segs:
+        end = pos
+        while end < len(mine) and mine[end] in seg:
+            end += 1
+        for s in range(pos, end, k):
+            out = K.newton_schulz(work[s:min(s + k, end)], ns_steps)
+            K.muon_apply([(grp[mine[s + j]], out[j], scale, apply_seeds[mine[s + j]]) for j in range(out.shape[0])],
+                         lr, weight_decay)
+            del out
+        pos = end
+        if len(segs) > 1:
+            share([grp[i] for i in seg])
     del work
 
 
@@ -211,7 +244,8 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
                         self.state[p]["step"] = self._global_step
                 owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
                 muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd, step,
-                                seeder, owner, self._shard.share if self._shard else None)
+                                seeder, owner, self._shard.share if self._shard else None,
+                                self._shard.segments if self._shard else None)
             else:
                 for param_idx, p in enumerate(group["params"]):
                     assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
@@ -227,6 +261,8 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
                     if self._record_step:
                         state["step"] += 1
                     if self._shard and not self._shard.owns(gi, param_idx):
+                        seeder.skip(state.get("step", 0), param_idx, 0)
+                        seeder.skip(state.get("step", 0), param_idx, 1)
                         continue
                     muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
                                      state.get("step", 0), param_idx, seeder)
@@ -292,9 +328,10 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
             offsets.append(total)
             total += len(group["params"])
         order = list(range(len(self.param_groups)))
-        if self._shard:
+        if self._shard and not self._random_seeds:
             # AdamW groups (embedding, head) first so their broadcasts overlap the Muon work;
-            # every group's math is independent of the processing order.
+            # every group's math is independent of the processing order (seeds drawn from
+            # torch's generator are not: those classes keep the order).
             order.sort(key=lambda gi: bool(self.param_groups[gi]["use_muon"]))
         for gi in order:
             group = self.param_groups[gi]
@@ -322,7 +359,8 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                             self.state[p]["step"] = self._global_step
                     owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
                     muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd,
-                                    step, seeder, owner, self._shard.share if self._shard else None)
+                                    step, seeder, owner, self._shard.share if self._shard else None,
+                                    self._shard.segments if self._shard else None)
                 else:
                     for param_idx, p in enumerate(group["params"]):
                         assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
@@ -338,6 +376,8 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                         if self._record_muon_step:
                             state["step"] += 1
                         if self._shard and not self._shard.owns(gi, param_idx):
+                            seeder.skip(state.get("step", 0), param_idx, 0)
+                            seeder.skip(state.get("step", 0), param_idx, 1)
                             continue
                         muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
                                          state.get("step", 0), param_idx, seeder)
@@ -360,10 +400,10 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
                         state["ema"] = torch.zeros_like(p, dtype=torch.bfloat16)
                         state["ema_squared"] = torch.zeros_like(p, dtype=torch.bfloat16)
                     state["step"] += 1
+                    seed = seeder(state["step"], group_offset + i, 0)
                     if self._shard and not self._shard.owns(gi, i):
                         continue
-                    items.append((p, _grad_of(p), state["ema"], state["ema_squared"], state["step"],
-                                  seeder(state["step"], group_offset + i, 0)))
+                    items.append((p, _grad_of(p), state["ema"], state["ema_squared"], state["step"], seed))
                 K.adamw_sr(items, lr, beta1, beta2, eps, wd)
                 if self._shard:
                     self._shard.share(group["params"])

@@ -3,16 +3,16 @@
 The reference is single-device; data-parallel replicas each run the whole optimizer step
 and stay identical because the rounding seeds depend only on (step, index). Here each rank
 runs the step for the parameters it owns and the updated bf16 weights are then shared over
-NCCL (NVLink / NVSwitch), so the step's work is divided by the number of ranks.
+NVLink / NVSwitch, so the step's work is divided by the number of ranks.
 
 * Partition: whole tensors (Newton-Schulz needs each full matrix), longest-processing-time
   greedy on an estimated B200 time per tensor -- Newton-Schulz FLOPs at the tensor-core rate
   for Muon matrices, bytes at the HBM rate for AdamW / 8-bit tensors.
 * Seeds and Philox counters stay global, so every rank writes exactly the bits a single GPU
   would (Newton-Schulz computes each matrix independently of how the batch is chunked).
-* Sharing: as soon as a shape stack (or param group) is updated, its parameters are
-  broadcast from their owners on NCCL's stream, so the transfers run under the next
-  stacks' Newton-Schulz work; the step ends by waiting for all of them.
+* Sharing: as soon as a segment of a shape stack (or a param group) is updated, its
+  parameters travel from their owners (see ``transport``), so the transfers run under the
+  remaining Newton-Schulz work; the step ends by waiting for all of them.
 * Optimizer state (momentum, moments) stays with the owner; ``state_dict()`` on a rank holds
   valid values only for the parameters that rank owns until ``gather_state`` copies the
   owners' values over (for checkpoints).
@@ -27,6 +27,8 @@ import torch.distributed as dist
 
 TENSOR_FLOPS = 1.4e15   # sustained dense bf16 on B200, used only to weigh the partition
 HBM_BYTES = 6.5e12
+SEGMENT_SECONDS = 4e-3  # per-rank Newton-Schulz time between two weight shares of a stack
+COPY_STREAMS_PER_PEER = 2
 
 
 def _ns_flops(shape, steps=5):
@@ -129,6 +131,13 @@ class Sharder:
                 self.transport = "nccl"
         self.begin_step()
         return self
+
+    def segments(self, shape, n) -> int:
+        """Number of consecutive segments a stack of ``n`` matrices of ``shape`` is shared
+        in: about SEGMENT_SECONDS of Newton-Schulz per rank each, at least two matrices per
+        rank per segment (so the batched GEMMs stay full), at most 8."""
+        per_rank = n * _ns_flops(tuple(shape)) / TENSOR_FLOPS / self.world
+        return max(1, min(8, n // (2 * self.world), round(per_rank / SEGMENT_SECONDS)))
 
     def owns(self, gi, pi) -> bool:
         return self._owner[id(self._groups[gi]["params"][pi])] == self.rank
@@ -291,7 +300,10 @@ class _PeerMaps:
                     opened[(r, h)] = base.value
                     self.bases.append(base.value)
                 self.remote[i] = opened[(r, h)] + off
-        self.streams = {r: torch.cuda.Stream(self.device) for r in range(sh.world) if r != sh.rank}
+        # several copy streams per owner spread the transfers over more copy engines
+        self.streams = {r: [torch.cuda.Stream(self.device) for _ in range(COPY_STREAMS_PER_PEER)]
+                        for r in range(sh.world) if r != sh.rank}
+        self.next_stream = {r: 0 for r in self.streams}
         self.owned_events = []
         self.events = []      # per share point: (local event, {rank: peer event})
         self.done = self._event_set()
@@ -327,10 +339,13 @@ class _PeerMaps:
             r = self.sh._owner[id(p)]
             if r == self.sh.rank:
                 continue
-            s = self.streams[r]
             if r not in waited:
-                self._check(self.lib.msr_stream_wait_event(ctypes.c_void_p(s.cuda_stream), ctypes.c_void_p(peers[r])))
+                for s in self.streams[r]:
+                    self._check(self.lib.msr_stream_wait_event(ctypes.c_void_p(s.cuda_stream),
+                                                               ctypes.c_void_p(peers[r])))
                 waited.add(r)
+            s = self.streams[r][self.next_stream[r]]
+            self.next_stream[r] = (self.next_stream[r] + 1) % len(self.streams[r])
             nbytes = p.numel() * p.element_size()
             self._check(self.lib.msr_copy_async(ctypes.c_void_p(p.data_ptr()),
                                                 ctypes.c_void_p(self.remote[self.sh._index[id(p)]]), nbytes,
@@ -344,8 +359,9 @@ class _PeerMaps:
 
     def finish(self):
         main = torch.cuda.current_stream(self.device)
-        for s in self.streams.values():
-            main.wait_stream(s)
+        for ss in self.streams.values():
+            for s in ss:
+                main.wait_stream(s)
         ev, peers = self.done
         # this rank's copies of its peers' weights are done ...
         self._check(self.lib.msr_event_record(ctypes.c_void_p(ev), ctypes.c_void_p(main.cuda_stream)))

@@ -2,7 +2,8 @@
 
 Each rank updates only the tensors the Sharder assigns to it and receives the others over
 NVLink; seeds and Philox counters are global and Newton-Schulz computes each matrix on its
-own, so the parameters after every step must equal a 1-GPU run bit for bit. The gradients
+own, so the parameters after every step must equal a 1-GPU run bit for bit (also when
+stacks are shared segment by segment, and for the random-seed classes). The gradients
 start rank-local and reach their owners through ``reduce_grads``; after the steps
 ``gather_state`` must reproduce the single-GPU optimizer state (checkpoint interop).
 Skipped on a box with fewer than 2 GPUs.
@@ -15,7 +16,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-SHAPES_MUON = [(256, 512)] * 3 + [(512, 256)] * 2 + [(128, 384)] * 2
+SHAPES_MUON = [(256, 512)] * 9 + [(512, 256)] * 2 + [(128, 384)] * 2
 SHAPES_ADAM = [(1000, 64), (64,), (64,)]
 
 
@@ -64,12 +65,26 @@ def _run(device, shard, steps=3, batch_ns=True, rank=0):
         if sh8 is not None:
             sh8.reduce_grads(opt8)
         opt8.step()
+    # the random-seed variant: every process draws its seeds from an identically seeded
+    # torch generator, ranks skip (but still draw) the seeds of tensors they do not own
+    from muon_sr_b200 import MuonSRWithAuxAdam
+    muon_r = [torch.nn.Parameter(p.detach().clone()) for p in muon]
+    adam_r = [torch.nn.Parameter(p.detach().clone()) for p in adam]
+    sh_r = shard() if shard else None
+    opt_r = MuonSRWithAuxAdam([dict(params=muon_r, use_muon=True), dict(params=adam_r, use_muon=False)],
+                              batch_ns=batch_ns, shard=sh_r)
+    torch.manual_seed(1234)
+    for k in range(2):
+        for p, g in zip(muon_r + adam_r, _grads(20 + k, device)):
+            p.grad = g
+        opt_r.step()
     if sh is not None:
         sh.gather_state(opt)
         sh8.gather_state(opt8)
     torch.cuda.synchronize()
     state = _state_tensors(opt) + _state_tensors(opt8)
-    return [p.detach().cpu() for p in muon + adam + params8] + [t.detach().cpu() for t in state]
+    return ([p.detach().cpu() for p in muon + adam + params8] + [t.detach().cpu() for t in state] +
+            [p.detach().cpu() for p in muon_r + adam_r])
 
 
 def _bits(t):
@@ -79,7 +94,8 @@ def _bits(t):
 
 def _worker(rank, world, port, q):
     import torch.distributed as dist
-    from muon_sr_b200 import Sharder
+    from muon_sr_b200 import Sharder, sharding
+    sharding.SEGMENT_SECONDS = 1e-9  # share the larger stacks in segments even at these sizes
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
