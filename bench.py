@@ -27,6 +27,10 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# The sharded step's peer copies run on 2 streams per peer next to the compute stream; with
+# CUDA's default 8 hardware queues a copy stream waiting on a peer's event can hold up the
+# compute stream that shares its queue. Must be set before CUDA initialises.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
 
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
@@ -214,6 +218,14 @@ def run_ours(args, rank, world, local_rank):
     clocks = sampler.stop()
     tot = timers.totals_ms()
     timers.enabled = False
+    # host time to issue one step (the device still works on the previous one)
+    host = []
+    for _ in range(2):
+        t0 = time.perf_counter()
+        opt.step()
+        host.append((time.perf_counter() - t0) * 1e3)
+    torch.cuda.synchronize()
+    host_ms = min(host)
     assert K.device_error() == 0, "device wait timed out in a kernel"
 
     # Newton-Schulz roofline: algorithmic FLOPs of the matrices this rank owned
@@ -230,6 +242,7 @@ def run_ours(args, rank, world, local_rank):
     n_muon = sum(p.numel() for p in muon)
     n_adam = sum(p.numel() for p in adam)
     breakdown = {k: v / args.steps for k, v in tot.items()}
+    breakdown["host_issue"] = host_ms
     per_rank = [breakdown]
     if world > 1:
         per_rank = [None] * world

@@ -21,6 +21,8 @@ NVLink / NVSwitch, so the step's work is divided by the number of ranks.
 """
 import ctypes
 import heapq
+import os
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -54,8 +56,9 @@ class Sharder:
 
     * ``"p2p"`` (default on CUDA): every rank maps, once, the device allocations that hold
       the parameters other ranks own (CUDA IPC) and pulls their updated values with
-      copy-engine peer copies over NVLink on one side stream per owner, so the transfers use
-      no SMs and run under the Newton-Schulz GEMMs. Ordering: after each shape stack every
+      copy-engine peer copies over NVLink on COPY_STREAMS_PER_PEER side streams per owner, so
+      the transfers use no SMs and run under the Newton-Schulz GEMMs (the process needs
+      CUDA_DEVICE_MAX_CONNECTIONS=32 so that these streams get their own hardware queues). Ordering: after each shape stack every
       rank records an interprocess event on its compute stream, a host-only (gloo) barrier
       makes sure all records are enqueued, and the copies wait on the owners' events; at the
       end of the step the compute stream waits for the copies and for the peers' copies of
@@ -80,6 +83,10 @@ class Sharder:
             sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
             _lib.load().msr_set_gemm_max_ctas(max(1, sms - int(reserve_sms)))
         self.transport = transport if torch.cuda.is_available() else "nccl"
+        if self.transport == "p2p" and int(os.environ.get("CUDA_DEVICE_MAX_CONNECTIONS", "8")) < 8 * COPY_STREAMS_PER_PEER:
+            warnings.warn("Sharder(transport='p2p') runs several copy streams per peer next to the compute stream; "
+                          "set CUDA_DEVICE_MAX_CONNECTIONS=32 before CUDA initialises, or copies waiting on peers "
+                          "can delay compute kernels that share their hardware queue", RuntimeWarning)
         # host-only barriers for the p2p ordering (created collectively, same order on all ranks)
         self._host = dist.new_group(backend="gloo") if self.transport == "p2p" else None
         self._owner = None  # id(param) -> rank within the group
