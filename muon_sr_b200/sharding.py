@@ -58,7 +58,8 @@ class Sharder:
       the parameters other ranks own (CUDA IPC) and pulls their updated values with
       copy-engine peer copies over NVLink on COPY_STREAMS_PER_PEER side streams per owner, so
       the transfers use no SMs and run under the Newton-Schulz GEMMs (the process needs
-      CUDA_DEVICE_MAX_CONNECTIONS=32 so that these streams get their own hardware queues). Ordering: after each shape stack every
+      CUDA_DEVICE_MAX_CONNECTIONS=32 so that these streams get their own hardware queues).
+      Ordering: at each share point every
       rank records an interprocess event on its compute stream, a host-only (gloo) barrier
       makes sure all records are enqueued, and the copies wait on the owners' events; at the
       end of the step the compute stream waits for the copies and for the peers' copies of

@@ -96,7 +96,8 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
     from muon_sr_b200 import Sharder, sharding
     sharding.SEGMENT_SECONDS = 1e-9  # share the larger stacks in segments even at these sizes
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      CUDA_DEVICE_MAX_CONNECTIONS="32")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
