@@ -42,8 +42,16 @@ const char* msr_status_string(int status);
 /* Detail message of the last failing call on the calling host thread ("" if none). */
 const char* msr_last_error(void);
 /* Synchronises `stream`, returns the device-side error code recorded by any kernel of
- * this library since the last clear (0 = none) and clears it when `clear` != 0. */
+ * this library since the last clear (0 = none) and clears it when `clear` != 0. Codes: the
+ * first wait that ran out of time, 0x101 / 0x102 / 0x103 for the GEMM's copy, MMA and
+ * epilogue roles, 0x1FF for msr_test_wait_timeout. Every device-side wait of this library
+ * is bounded (1 s); a kernel that gives up drains its own copies, frees its tensor memory
+ * and returns, so the context stays usable. */
 int msr_device_error(msr_stream_t stream, int clear);
+/* Failure-detection test hook (no counterpart in the reference): launches one kernel that
+ * waits, with the GEMM's bounded wait, on a barrier nothing arrives on and gives up after
+ * `limit_ns` (at most 10 s), recording 0x1FF for msr_device_error. */
+int msr_test_wait_timeout(uint64_t limit_ns, msr_stream_t stream);
 /* Number of kernels this library has launched in this process (all threads, all devices). */
 uint64_t msr_launch_count(void);
 /* Caps the number of CTAs (one per SM) of the persistent GEMM kernels; 0 = one per SM (the
@@ -130,6 +138,14 @@ typedef struct msr_adamw_hparams {
 
 int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp,
                  msr_stream_t stream);
+
+/* Gradient centralisation for TritonAdamW's `centralization` option: grad viewed as
+ * [rows][cols] (rows = leading dim, or 1 for a vector), out = bf16_rne(g - c * mean_row)
+ * with the row mean in fp32. One read of the gradient, one bf16 write (out must not
+ * overlap grad). Replaces the torch ops of muon_sr/triton_adamw.py:179-187; the fp32 mean
+ * is summed in a fixed order, which can differ from torch's reduction in its last bit. */
+int msr_centralize_bf16(const void* grad, void* out, int64_t rows, int64_t cols, float centralization,
+                        msr_stream_t stream);
 
 /* ---- 8-bit blockwise AdamW -----------------------------------------------------------
  * One pass per tensor: dequantise (codebook x block absmax), Adam moments with the

@@ -59,6 +59,7 @@ SIGNATURES = [
     ("msr_status_string", ctypes.c_char_p, [c_int]),
     ("msr_last_error", ctypes.c_char_p, []),
     ("msr_device_error", c_int, [c_void_p, c_int]),
+    ("msr_test_wait_timeout", c_int, [c_uint64, c_void_p]),
     ("msr_launch_count", c_uint64, []),
     ("msr_set_gemm_max_ctas", None, [c_int]),
     ("msr_set_gemm_pairs", None, [c_int]),
@@ -67,6 +68,7 @@ SIGNATURES = [
     ("msr_muon_prepare", c_int, [ctypes.POINTER(PrepareEntry), c_int, c_float, c_float, c_int, c_void_p]),
     ("msr_muon_apply", c_int, [ctypes.POINTER(ApplyEntry), c_int, c_float, c_float, c_void_p]),
     ("msr_adamw_sr", c_int, [ctypes.POINTER(AdamWEntry), c_int, ctypes.POINTER(AdamWHparams), c_void_p]),
+    ("msr_centralize_bf16", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     ("msr_adamw8bit", c_int, [ctypes.POINTER(Adam8Entry), c_int, c_void_p, c_void_p,
                               ctypes.POINTER(Adam8Hparams), c_void_p]),
     ("msr_ns_workspace_bytes", c_size_t, [c_int64, c_int64, c_int64]),

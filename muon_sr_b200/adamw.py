@@ -55,11 +55,9 @@ class TritonAdamW(Optimizer):
                     state["ema_squared"] = torch.zeros_like(p.data, dtype=torch.bfloat16)
                 state["step"] += 1
                 # Gradient centralization (triton_adamw.py:179-187): a per-row mean over all
-                # trailing dims, subtracted in fp32, rounded back to bf16.
+                # trailing dims, subtracted in fp32, rounded back to bf16 -- one fused kernel.
                 if centralization != 0:
-                    g32 = grad.to(torch.float32)
-                    g32.sub_(g32.mean(dim=tuple(range(1, g32.dim())), keepdim=True).mul_(centralization))
-                    grad = g32.to(torch.bfloat16)
+                    grad = K.centralize(grad, centralization)
                 if not grad.is_contiguous():
                     grad = grad.contiguous()
                 items.append((p, grad, state["ema"], state["ema_squared"], state["step"],

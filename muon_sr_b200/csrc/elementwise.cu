@@ -329,6 +329,57 @@ __global__ __launch_bounds__(EW_THREADS, 2) void adamw_kernel(const __grid_const
   }
 }
 
+// Gradient centralisation -- muon_sr/triton_adamw.py:179-187: out = bf16(g - c * mean), the
+// mean taken in fp32 over all trailing dims of each leading index (over all elements for a
+// vector), rounded to nearest-even as the reference's .to(bfloat16). One CTA per row: the
+// row is summed in a fixed order (deterministic) and read again, from cache, for the output.
+constexpr int CT_THREADS = 256;
+
+__global__ __launch_bounds__(CT_THREADS) void centralize_kernel(const uint16_t* __restrict__ g,
+                                                                uint16_t* __restrict__ out, int64_t rows,
+                                                                int64_t cols, float c, int vec) {
+  __shared__ float red[CT_THREADS / 32];
+  __shared__ float mean_s;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t* gr = g + r * cols;
+    uint16_t* orow = out + r * cols;
+    float s = 0.f;
+    if (vec) {
+      for (int64_t i = threadIdx.x * 8; i < cols; i += CT_THREADS * 8) {
+        const U16x8 w = ld_u16x8(gr + i);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s = __fadd_rn(s, bf16_bits_to_f32(w.v[j]));
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < cols; i += CT_THREADS) s = __fadd_rn(s, bf16_bits_to_f32(gr[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < CT_THREADS / 32; ++w) t = __fadd_rn(t, red[w]);
+      mean_s = __fdiv_rn(t, static_cast<float>(cols));
+    }
+    __syncthreads();
+    const float cm = __fmul_rn(mean_s, c);
+    if (vec) {
+      for (int64_t i = threadIdx.x * 8; i < cols; i += CT_THREADS * 8) {
+        U16x8 w = ld_u16x8(gr + i);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w.v[j] = rne_bf16_bits(__fsub_rn(bf16_bits_to_f32(w.v[j]), cm));
+        st_u16x8(orow + i, w);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < cols; i += CT_THREADS)
+        orow[i] = rne_bf16_bits(__fsub_rn(bf16_bits_to_f32(gr[i]), cm));
+    }
+    __syncthreads();  // red / mean_s are reused by the next row
+  }
+}
+
 inline bool ptr_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline int grid_for(int64_t chunks) {
@@ -349,6 +400,19 @@ int msr_philox_fill(uint32_t* out, int64_t n, uint64_t ctr_base, uint64_t key, m
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
   philox_fill_kernel<<<blocks, 256, 0, to_stream(stream)>>>(out, n, ctr_base, make_key(key));
   return check_launch("philox_fill_kernel");
+}
+
+int msr_centralize_bf16(const void* grad, void* out, int64_t rows, int64_t cols, float centralization,
+                        msr_stream_t stream) {
+  if (!grad || !out || rows <= 0 || cols <= 0)
+    return fail(MSR_ERR_INVALID, "msr_centralize_bf16: null pointer or non-positive size");
+  if (int st = require_sm100()) return st;
+  const int vec = (cols % 8 == 0) && ptr_aligned16(grad) && ptr_aligned16(out);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(rows, 8 * (int64_t)sm_count())));
+  centralize_kernel<<<grid, CT_THREADS, 0, to_stream(stream)>>>(static_cast<const uint16_t*>(grad),
+                                                                static_cast<uint16_t*>(out), rows, cols,
+                                                                centralization, vec);
+  return check_launch("centralize_kernel");
 }
 
 int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, int first, msr_stream_t stream) {

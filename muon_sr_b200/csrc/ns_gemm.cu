@@ -465,6 +465,23 @@ struct SharedStorage {
 };
 }  // namespace pair
 
+// Failure-detection test hook: one thread waits, through the same bounded wait the GEMM
+// roles use, on an mbarrier that nothing arrives on, and records ERR_TEST_WAIT when the
+// limit runs out; the kernel then returns normally and the context stays usable.
+constexpr int ERR_TEST_WAIT = 0x1FF;
+
+__global__ void wait_timeout_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !tc::mbar_wait(&bar, 0, &abort_flag, limit_ns)) record_error(ERR_TEST_WAIT);
+}
+
 // Sleeps for about `ns` nanoseconds of wall time.
 __device__ __forceinline__ void settle(uint64_t ns) {
   uint64_t t0, t;
@@ -963,6 +980,14 @@ extern "C" {
 void msr_set_gemm_max_ctas(int max_ctas) { g_gemm_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
 
 void msr_set_gemm_pairs(int enable) { g_gemm_pairs.store(enable ? 1 : 0); }
+
+int msr_test_wait_timeout(uint64_t limit_ns, msr_stream_t stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(MSR_ERR_INVALID, "msr_test_wait_timeout: limit must be in (0, 10 s]");
+  if (int st = require_sm100()) return st;
+  wait_timeout_kernel<<<1, 32, 0, to_stream(stream)>>>(limit_ns);
+  return check_launch("wait_timeout_kernel");
+}
 
 int msr_device_error(msr_stream_t stream, int clear) {
   cudaError_t e = cudaStreamSynchronize(to_stream(stream));

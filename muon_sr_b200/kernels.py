@@ -222,6 +222,22 @@ def gemm_bf16(a, a_mn_major, b, b_mn_major, c=None, alpha=1.0, beta=0.0, scale=N
     return d
 
 
+def centralize(grad: torch.Tensor, centralization: float) -> torch.Tensor:
+    """``bf16(g - c * g.mean(dim=trailing dims, keepdim=True))`` with the mean in fp32, as
+    TritonAdamW's centralization (muon_sr/triton_adamw.py:179-187), in one fused kernel;
+    returns a new bf16 tensor."""
+    g = grad if grad.is_contiguous() else grad.contiguous()
+    _require(g, "grad")
+    out = torch.empty_like(g, memory_format=torch.contiguous_format)
+    if g.numel() == 0:
+        return out
+    rows = g.shape[0] if g.dim() > 1 else 1
+    _lib.check(_lib.load().msr_centralize_bf16(g.data_ptr(), out.data_ptr(), rows, g.numel() // rows,
+                                               float(centralization), stream_handle(g.device)),
+               "msr_centralize_bf16")
+    return out
+
+
 def set_gemm_pairs(enable: bool) -> None:
     """Run the Newton-Schulz GEMMs on SM pairs (256 x 256 tiles, the default) or on single
     SMs (128 x 256 tiles). Both produce the same bits; process-wide."""

@@ -233,3 +233,24 @@ def test_sr_statistics_256_seeds():
     assert (z[~exact] < 3.0).mean() > 0.99, "SR mean drifts from the fp32 value"
     assert np.all(mean[exact] == x[exact])
     del down
+
+
+@pytest.mark.parametrize("shape", [(1000, 768), (37, 100), (5000,), (3, 4, 5), (2, 8)])
+def test_centralize_matches_reference_ops(shape):
+    """The fused centralisation kernel against the reference's torch ops
+    (muon_sr/triton_adamw.py:179-187) on the same GPU: bf16(g - c * mean_row) with the mean in
+    fp32. Only the fp32 mean's summation order differs, so an element may differ by one bf16
+    ulp, on a small fraction of elements."""
+    g = (torch.randn(*shape, device="cuda") * 1e-3).bfloat16()
+    g[..., 0] += 5e-3  # rows with a clear nonzero mean
+    g0 = g.clone()
+    got = K.centralize(g, 0.5)
+    g32 = g.to(torch.float32)
+    g32.sub_(g32.mean(dim=tuple(range(1, g32.dim())), keepdim=True).mul_(0.5))
+    want = g32.to(torch.bfloat16)
+    gi = got.view(torch.int16).int()
+    wi = want.view(torch.int16).int()
+    diff = (gi - wi).abs()
+    assert int(diff.max()) <= 1
+    assert float((diff > 0).float().mean()) < 0.02
+    assert torch.equal(g, g0)  # the gradient itself is not modified
