@@ -183,7 +183,6 @@ def time_steps(step_fn, steps, warmup, world):
 def run_ours(args, rank, world, local_rank):
     from muon_sr_b200 import Sharder, TritonAdamW8bit, TritonMuonSRWithAuxAdam, _lib
     from muon_sr_b200 import kernels as K
-    from muon_sr_b200 import muon as M
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)

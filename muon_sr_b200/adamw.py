@@ -12,6 +12,39 @@ from . import kernels as K
 from .seeds import deterministic_seed
 
 
+def adamw_group_step(state, group, offset, seed_of, owns=None, centralization=0.0):
+    """The AdamW-SR update of one param group (``_adamw_kernel`` launches,
+    triton_adamw.py:9-114, and the hybrid's AdamW groups, triton_muon_sr.py:356-371).
+
+    Per parameter with a gradient: state ``step``/``ema``/``ema_squared`` (created at zero),
+    the step advanced, the seed ``seed_of(step, offset + i)`` with ``offset`` the number of
+    parameters in earlier groups; then the whole group in one multi-tensor launch. ``owns(i)``
+    restricts the kernel work to this rank's parameters (state and seeds still advance, so
+    every rank stays in step). ``centralization`` != 0 first centres each gradient with the
+    fused kernel (triton_adamw.py:179-187)."""
+    beta1, beta2 = group["betas"]
+    batch = []
+    for i, p in enumerate(group["params"]):
+        assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+        if p.grad is None:
+            continue
+        if p.grad.is_sparse:
+            raise RuntimeError("TritonAdamW does not support sparse gradients")
+        st = state[p]
+        if not st:
+            st.update(step=0, ema=torch.zeros_like(p, dtype=torch.bfloat16),
+                      ema_squared=torch.zeros_like(p, dtype=torch.bfloat16))
+        st["step"] += 1
+        seed = seed_of(st["step"], offset + i)
+        if owns is not None and not owns(i):
+            continue
+        if p.grad.dtype != torch.bfloat16:
+            raise ValueError("gradients must be bfloat16")
+        grad = K.centralize(p.grad, centralization) if centralization else p.grad.contiguous()
+        batch.append((p, grad, st["ema"], st["ema_squared"], st["step"], seed))
+    K.adamw_sr(batch, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
+
+
 class TritonAdamW(Optimizer):
     r"""AdamW with stochastic rounding as one fused multi-tensor kernel per param group.
 
@@ -34,35 +67,11 @@ class TritonAdamW(Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        param_offset = 0
+        offset = 0
         for group in self.param_groups:
-            group_offset = param_offset
-            param_offset += len(group["params"])
-            beta1, beta2 = group["betas"]
-            centralization = group["centralization"]
-            items = []
-            for i, p in enumerate(group["params"]):
-                assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
-                if p.grad is None:
-                    continue
-                grad = p.grad
-                if grad.is_sparse:
-                    raise RuntimeError("TritonAdamW does not support sparse gradients")
-                state = self.state[p]
-                if len(state) == 0:
-                    state["step"] = 0
-                    state["ema"] = torch.zeros_like(p.data, dtype=torch.bfloat16)
-                    state["ema_squared"] = torch.zeros_like(p.data, dtype=torch.bfloat16)
-                state["step"] += 1
-                # Gradient centralization (triton_adamw.py:179-187): a per-row mean over all
-                # trailing dims, subtracted in fp32, rounded back to bf16 -- one fused kernel.
-                if centralization != 0:
-                    grad = K.centralize(grad, centralization)
-                if not grad.is_contiguous():
-                    grad = grad.contiguous()
-                items.append((p, grad, state["ema"], state["ema_squared"], state["step"],
-                              deterministic_seed(state["step"], group_offset + i)))
-            K.adamw_sr(items, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
+            adamw_group_step(self.state, group, offset, deterministic_seed,
+                             centralization=group["centralization"])
+            offset += len(group["params"])
         return loss
 
 

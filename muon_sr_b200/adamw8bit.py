@@ -15,22 +15,65 @@ from . import kernels as K
 
 
 def create_dynamic_map(signed=True):
-    """The 256-entry dynamic (signed) / unsigned-dynamic codebook
-    (muon_sr/triton_adamw_8bit.py:14-25: per decade i = 0..6, the midpoints of
-    linspace(0.1, 1, 2^i + 1) -- 2^(i+1) + 1 for unsigned -- scaled by 10^(i-6), both signs
-    for the signed map, plus 0 and 1, sorted)."""
-    data = []
-    for i in range(7):
-        boundaries = torch.linspace(0.1, 1, 2 ** (i if signed else i + 1) + 1, dtype=torch.float32)
-        means = (boundaries[:-1] + boundaries[1:]) / 2
-        data.extend((10 ** (-6 + i) * means).tolist())
-        if signed:
-            data.extend((-10 ** (-6 + i) * means).tolist())
-    return torch.tensor(sorted(data + [0., 1.]), dtype=torch.float32)
+    """The 256-entry dynamic codebook of ``muon_sr.triton_adamw_8bit.create_dynamic_map``
+    (triton_adamw_8bit.py:14-25), bit for bit.
+
+    Decade k = 0..6 covers [0.1, 1) x 10^(k-6) with the midpoints of an fp32 ``linspace``
+    grid of 2^k intervals (2^(k+1) for the unsigned map, which has no negative half); the
+    signed map mirrors every value; 0 and 1 are added and the table is sorted."""
+    half = []
+    for decade in range(7):
+        intervals = 1 << (decade if signed else decade + 1)
+        edges = torch.linspace(0.1, 1, intervals + 1, dtype=torch.float32)
+        mids = (edges[:-1] + edges[1:]) / 2
+        half.append(10 ** (decade - 6) * mids)
+    pos = torch.cat(half)
+    table = torch.cat([pos, -pos]) if signed else pos
+    table = torch.cat([table, torch.tensor([0.0, 1.0])])
+    return table.sort().values.to(torch.float32)
 
 
-def _cdiv(a, b):
-    return (a + b - 1) // b
+def _blocks(numel, block):
+    return -(-numel // block)
+
+
+def _bits_for(p, group):
+    """Moment width of a parameter: tensors below min_8bit_size always keep bf16 moments."""
+    return 16 if p.numel() < group['min_8bit_size'] else group['optim_bits']
+
+
+def _state_spec(p, group):
+    """(shape, dtype) of every tensor the optimizer keeps for ``p`` -- one definition for
+    state creation and checkpoint validation."""
+    if _bits_for(p, group) == 16:
+        return {'state1': (tuple(p.shape), torch.bfloat16), 'state2': (tuple(p.shape), torch.bfloat16)}
+    nblk = (_blocks(p.numel(), group['block_size']),)
+    return {'state1': (tuple(p.shape), torch.uint8), 'state2': (tuple(p.shape), torch.uint8),
+            'qmap1': ((256,), torch.float32), 'qmap2': ((256,), torch.float32),
+            'absmax1': (nblk, torch.float32), 'absmax2': (nblk, torch.float32)}
+
+
+_TENSOR_KEYS = ('state1', 'state2', 'qmap1', 'qmap2', 'absmax1', 'absmax2')
+
+
+def _check_group(g):
+    """The reference's group rules (triton_adamw_8bit.py:138-150), raising ValueError."""
+    for key in ('lr', 'eps', 'weight_decay'):
+        v = g[key]
+        if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v) or v < 0:
+            raise ValueError(f'{key} must be a finite number >= 0, got {v!r}')
+    if g['eps'] == 0:
+        raise ValueError('eps must be positive')
+    betas = g['betas']
+    if len(betas) != 2 or not all(0 <= b < 1 for b in betas):
+        raise ValueError(f'betas must be two values in [0, 1), got {betas!r}')
+    block = g['block_size']
+    if not isinstance(block, int) or not 32 <= block <= 4096 or block & (block - 1):
+        raise ValueError(f'block_size must be a power of two in [32, 4096], got {block!r}')
+    if g['optim_bits'] not in (8, 16):
+        raise ValueError(f"optim_bits must be 8 or 16, got {g['optim_bits']!r}")
+    if not isinstance(g['min_8bit_size'], int) or g['min_8bit_size'] < 0:
+        raise ValueError(f"min_8bit_size must be an int >= 0, got {g['min_8bit_size']!r}")
 
 
 class TritonAdamW8bit(Optimizer):
@@ -49,53 +92,44 @@ class TritonAdamW8bit(Optimizer):
         self._qtables = {}
         self._shard = shard
         for group in self.param_groups:
-            self._validate_group(group)
+            _check_group(group)
 
     @classmethod
     def for_model(cls, model, min_8bit_size=4096, **kwargs):
-        """Embeddings (including tied heads) and tensors below min_8bit_size get 16-bit
-        states (muon_sr/triton_adamw_8bit.py:119-136)."""
+        """Two groups: 16-bit moments for embedding weights (a tied output head is the same
+        tensor) and tensors below min_8bit_size, 8-bit for the rest
+        (triton_adamw_8bit.py:119-136)."""
         if 'optim_bits' in kwargs:
-            raise ValueError('for_model selects optim_bits per group')
-        embeddings = {id(p) for mod in model.modules() if isinstance(mod, torch.nn.Embedding)
-                      for p in mod.parameters()}
-        groups = {8: [], 16: []}
-        for p in model.parameters():
-            if p.requires_grad:
-                bits = 16 if id(p) in embeddings or p.numel() < min_8bit_size else 8
-                groups[bits].append(p)
-        return cls([dict(params=params, optim_bits=bits) for bits, params in groups.items() if params],
-                   min_8bit_size=min_8bit_size, **kwargs)
+            raise ValueError('for_model chooses optim_bits itself; pass it per group to the constructor instead')
+        embedding_ids = set()
+        for module in model.modules():
+            if isinstance(module, torch.nn.Embedding):
+                embedding_ids.update(id(t) for t in module.parameters())
+        wide, narrow = [], []
+        for t in model.parameters():
+            if not t.requires_grad:
+                continue
+            (wide if id(t) in embedding_ids or t.numel() < min_8bit_size else narrow).append(t)
+        groups = [dict(params=ts, optim_bits=bits) for bits, ts in ((8, narrow), (16, wide)) if ts]
+        return cls(groups, min_8bit_size=min_8bit_size, **kwargs)
 
-    @staticmethod
-    def _validate_group(g):
-        """muon_sr/triton_adamw_8bit.py:138-150."""
-        for key in ('lr', 'eps', 'weight_decay'):
-            v = g[key]
-            if not isinstance(v, (int, float)) or not math.isfinite(v) or v < 0:
-                raise ValueError(f'{key} must be a finite nonnegative scalar')
-        if g['eps'] == 0 or len(g['betas']) != 2 or any(not 0 <= b < 1 for b in g['betas']):
-            raise ValueError('eps must be positive and betas must be in [0,1)')
-        block = g['block_size']
-        if not isinstance(block, int) or block < 32 or block > 4096 or block & (block - 1):
-            raise ValueError('block_size must be a power of two between 32 and 4096')
-        if g['optim_bits'] not in (8, 16) or not isinstance(g['min_8bit_size'], int) or g['min_8bit_size'] < 0:
-            raise ValueError('optim_bits must be 8/16; min_8bit_size must be nonnegative')
+    def _codebooks(self, device):
+        if device not in self._maps:
+            self._maps[device] = (create_dynamic_map(True).to(device), create_dynamic_map(False).to(device))
+        return self._maps[device]
 
     def _init_state(self, p, group):
-        """muon_sr/triton_adamw_8bit.py:152-165."""
-        bits = 16 if p.numel() < group['min_8bit_size'] else group['optim_bits']
-        state = dict(step=0, format_version=2, block_size=group['block_size'], optim_bits=bits)
-        dtype = torch.uint8 if bits == 8 else torch.bfloat16
-        state.update(state1=torch.zeros_like(p, dtype=dtype), state2=torch.zeros_like(p, dtype=dtype))
-        if bits == 8:
-            if p.device not in self._maps:
-                self._maps[p.device] = (create_dynamic_map(True).to(p.device), create_dynamic_map(False).to(p.device))
-            state['qmap1'], state['qmap2'] = self._maps[p.device]
-            blocks = _cdiv(p.numel(), group['block_size'])
-            state['absmax1'] = torch.zeros(blocks, device=p.device, dtype=torch.float32)
-            state['absmax2'] = torch.zeros_like(state['absmax1'])
-            state['state1'].fill_(127)  # signed codebook's exact zero
+        """Fresh state (triton_adamw_8bit.py:152-165): zero moments -- code 127 is the signed
+        codebook's exact zero, code 0 the unsigned one's -- and zero block scales."""
+        spec = _state_spec(p, group)
+        state = dict(step=0, format_version=2, block_size=group['block_size'], optim_bits=_bits_for(p, group))
+        for key in ('state1', 'state2', 'absmax1', 'absmax2'):
+            if key in spec:
+                shape, dtype = spec[key]
+                state[key] = torch.zeros(shape, dtype=dtype, device=p.device)
+        if 'qmap1' in spec:
+            state['qmap1'], state['qmap2'] = self._codebooks(p.device)
+            state['state1'].fill_(127)
         return state
 
     @torch.no_grad()
@@ -108,7 +142,7 @@ class TritonAdamW8bit(Optimizer):
             self._shard.bind(self)
         index = 0
         for gi, group in enumerate(self.param_groups):
-            self._validate_group(group)
+            _check_group(group)
             b1, b2 = group['betas']
             by_maps = {}
             for pi, p in enumerate(group['params']):
@@ -126,9 +160,8 @@ class TritonAdamW8bit(Optimizer):
                 state = self.state[p]
                 if not state:
                     state.update(self._init_state(p, group))
-                expected_bits = 16 if p.numel() < group['min_8bit_size'] else group['optim_bits']
-                if state['block_size'] != group['block_size'] or state['optim_bits'] != expected_bits:
-                    raise ValueError('Cannot change quantization configuration after state initialization')
+                if state['block_size'] != group['block_size'] or state['optim_bits'] != _bits_for(p, group):
+                    raise ValueError('block_size / optim_bits of a group changed after its state was created')
                 state['step'] += 1
                 n = state['step']
                 if self._shard and not self._shard.owns(gi, pi):
@@ -154,40 +187,34 @@ class TritonAdamW8bit(Optimizer):
         return loss
 
     def load_state_dict(self, state_dict):
-        """Keeps uint8 codes and fp32 scales and validates the checkpoint
-        (muon_sr/triton_adamw_8bit.py:207-241)."""
-        groups = state_dict['param_groups']
-        if len(groups) != len(self.param_groups) or any(
-                len(a['params']) != len(b['params']) for a, b in zip(groups, self.param_groups)):
-            raise ValueError('Checkpoint parameter groups do not match optimizer')
-        mapping = dict(zip([i for g in groups for i in g['params']],
-                           [p for g in self.param_groups for p in g['params']]))
-        restored = {}
-        keys = {'state1', 'state2', 'qmap1', 'qmap2', 'absmax1', 'absmax2'}
-        for group in groups:
-            self._validate_group(group)
-            for ident in group['params']:
-                state = state_dict['state'].get(ident, {})
-                if not state:
+        """Checkpoint loading that keeps uint8 codes and fp32 scales (torch's default would cast
+        every state tensor to the parameter's dtype) and rejects checkpoints whose layout does
+        not match this optimizer's groups (triton_adamw_8bit.py:207-241)."""
+        saved_groups = state_dict['param_groups']
+        if [len(g['params']) for g in saved_groups] != [len(g['params']) for g in self.param_groups]:
+            raise ValueError('checkpoint param groups do not match this optimizer')
+        param_of = {}
+        for saved, live in zip(saved_groups, self.param_groups):
+            param_of.update(zip(saved['params'], live['params']))
+        kept = {}
+        for saved in saved_groups:
+            _check_group(saved)
+            for ident in saved['params']:
+                st = state_dict['state'].get(ident)
+                if not st:
                     continue
-                p = mapping[ident]
-                bits = 16 if p.numel() < group['min_8bit_size'] else group['optim_bits']
-                if state.get('format_version') != 2 or state.get('block_size') != group['block_size'] or \
-                        state.get('optim_bits') != bits:
-                    raise ValueError('Incompatible state format/quantization configuration')
-                specs = {key: (p.shape, torch.uint8 if bits == 8 else torch.bfloat16) for key in ('state1', 'state2')}
-                if bits == 8:
-                    specs.update({key: ((256,), torch.float32) for key in ('qmap1', 'qmap2')})
-                    specs.update({key: ((_cdiv(p.numel(), group['block_size']),), torch.float32)
-                                  for key in ('absmax1', 'absmax2')})
-                restored[ident] = {}
-                for key, (shape, dtype) in specs.items():
-                    value = state[key]
-                    if value.dtype != dtype or tuple(value.shape) != tuple(shape):
-                        raise ValueError(f'Invalid checkpoint state: {key}')
-                    restored[ident][key] = value.to(device=p.device, dtype=dtype).clone()
-        stripped = dict(state_dict, state={i: {k: v for k, v in state.items() if k not in keys}
-                                           for i, state in state_dict['state'].items()})
-        super().load_state_dict(stripped)
-        for ident, values in restored.items():
-            self.state[mapping[ident]].update(values)
+                p = param_of[ident]
+                layout = (st.get('format_version'), st.get('block_size'), st.get('optim_bits'))
+                if layout != (2, saved['block_size'], _bits_for(p, saved)):
+                    raise ValueError(f'checkpoint state of parameter {ident} has an incompatible layout {layout}')
+                kept[ident] = {}
+                for key, (shape, dtype) in _state_spec(p, saved).items():
+                    t = st[key]
+                    if t.dtype != dtype or tuple(t.shape) != shape:
+                        raise ValueError(f'checkpoint tensor {key} of parameter {ident} has dtype {t.dtype} and '
+                                         f'shape {tuple(t.shape)}, expected {dtype} {shape}')
+                    kept[ident][key] = t.to(device=p.device).clone()
+        rest = {i: {k: v for k, v in st.items() if k not in _TENSOR_KEYS} for i, st in state_dict['state'].items()}
+        super().load_state_dict(dict(state_dict, state=rest))
+        for ident, tensors in kept.items():
+            self.state[param_of[ident]].update(tensors)

@@ -935,8 +935,6 @@ int launch_normalize(const uint16_t* x, uint16_t* out, int64_t per, int64_t batc
 }
 
 inline int64_t round8(int64_t v) { return (v + 7) / 8 * 8; }
-struct NsLayout;
-int64_t xs_elems(const NsLayout& L);
 inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 struct NsLayout {
@@ -967,7 +965,6 @@ NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
   return L;
 }
 
-int64_t xs_elems(const NsLayout& L) { return L.R8 * L.C8; }
 
 }  // namespace gemm
 }  // namespace msr

@@ -8,17 +8,17 @@ keys and seed formulas (muon_sr/triton_muon_sr.py:180-373, muon_sr/muon_sr.py:23
   on the same CUDA kernels with seeds drawn from torch's default generator (the reference
   draws its rounding noise with ``torch.randint_like``), and keep those classes' state keys.
 
-Every step is: a multi-tensor prepare kernel (momentum, Nesterov, SR momentum, RNE update),
-the tcgen05 Newton-Schulz chain over each shape stack,
-and a multi-tensor apply kernel (decay, scaled update, SR weights). ``shard`` (optional)
-spreads the matrices over the ranks of a process group (see ``sharding``).
+A Muon update is: a multi-tensor prepare kernel (momentum, Nesterov, SR momentum, RNE
+update), the tcgen05 Newton-Schulz chain, and a multi-tensor apply kernel (decay, scaled
+update, SR weights). With ``batch_ns`` the momentum of equal-shaped matrices lives in one
+stack and Newton-Schulz runs on chunks of the stack. ``shard`` (optional) spreads the work
+over the ranks of a process group (see ``sharding``).
 """
-from collections import defaultdict
-
 import torch
 from torch.optim import Optimizer
 
 from . import kernels as K
+from .adamw import adamw_group_step
 from .seeds import deterministic_seed
 
 # Max elements per batched Newton-Schulz call, as in the reference (triton_muon_sr.py:125).
@@ -26,45 +26,49 @@ from .seeds import deterministic_seed
 NS_CHUNK_NUMEL = 1 << 28
 
 
-def _restore_global_step(state, groups):
-    """muon_sr/triton_muon_sr.py:13-15."""
-    return max((state[p].get("step", 0) for g in groups for p in g["params"]), default=0)
+# ---------------------------------------------------------------------------------------
+# Step state
+# ---------------------------------------------------------------------------------------
+class _MomentumStacks:
+    """Momentum of a batched Muon group: one bf16 ``[count, *shape]`` tensor per distinct
+    parameter shape (shapes in order of first appearance) with each parameter's
+    ``state["momentum_buffer"]`` a view of its row, so ``state_dict()`` still holds one buffer
+    per parameter (muon_sr/muon_sr.py:112-146). A buffer already present in the state (a
+    loaded checkpoint) is copied into its row."""
+
+    def __init__(self, params, state):
+        self.by_shape = {}
+        for p in params:
+            self.by_shape.setdefault(p.shape, []).append(p)
+        self.tensor = {}
+        self.row = {}
+        for shape, members in self.by_shape.items():
+            t = torch.zeros((len(members),) + tuple(shape), dtype=torch.bfloat16, device=members[0].device)
+            for r, p in enumerate(members):
+                self.row[id(p)] = r
+                loaded = state[p].get("momentum_buffer")
+                if loaded is not None:
+                    t[r].copy_(loaded)
+                state[p]["momentum_buffer"] = t[r]
+            self.tensor[shape] = t
 
 
-def _init_stacked_bufs(params, device, state):
-    """One bf16 [N, *shape] momentum stack per distinct shape; ``state[p]["momentum_buffer"]``
-    is a view into it (muon_sr/muon_sr.py:112-146)."""
-    shape_groups = defaultdict(list)
-    for p in params:
-        shape_groups[p.shape].append(p)
-    stacked_bufs, buf_indices = {}, {}
-    for shape, grp in shape_groups.items():
-        stacked = torch.zeros(len(grp), *shape, dtype=torch.bfloat16, device=device)
-        for i, p in enumerate(grp):
-            buf_indices[id(p)] = i
-            p_state = state[p]
-            if "momentum_buffer" in p_state:
-                stacked[i].copy_(p_state["momentum_buffer"])
-            p_state["momentum_buffer"] = stacked[i]
-        stacked_bufs[shape] = stacked
-    return dict(shape_groups), stacked_bufs, buf_indices
+class _GlobalStep:
+    """The batched groups' shared step counter (muon_sr/triton_muon_sr.py:13-15, 320-326): on
+    first use after construction or ``load_state_dict`` it resumes from the largest "step"
+    recorded in the state of those groups' parameters; it advances once per batched group
+    per ``step()`` call and is recorded in the state of every parameter of that group."""
 
+    def __init__(self):
+        self.value = None
 
-class _StackedBufsMixin:
-    """Stacked buffers and the global step live outside ``self.state``; rebuild them from
-    the loaded state on the next step (muon_sr/muon_sr.py:149-158)."""
-
-    def load_state_dict(self, state_dict):
-        super().load_state_dict(state_dict)
-        self._batch_state = {}
-        self.__dict__.pop("_global_step", None)
-
-
-def _grad_of(p):
-    g = p.grad
-    if g.dtype != torch.bfloat16:
-        raise ValueError("gradients must be bfloat16")
-    return g if g.is_contiguous() else g.contiguous()
+    def advance(self, state, groups, params):
+        if self.value is None:
+            self.value = max((state[p].get("step", 0) for g in groups for p in g["params"]), default=0)
+        self.value += 1
+        for p in params:
+            state[p]["step"] = self.value
+        return self.value
 
 
 class _Seeder:
@@ -84,6 +88,22 @@ class _Seeder:
         self(step, idx, salt)
 
 
+def _grad_of(p):
+    g = p.grad
+    if g.dtype != torch.bfloat16:
+        raise ValueError("gradients must be bfloat16")
+    return g if g.is_contiguous() else g.contiguous()
+
+
+def _validate(p, name):
+    assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
+    if p.grad is not None and p.grad.is_sparse:
+        raise RuntimeError(f"{name} does not support sparse gradients")
+
+
+# ---------------------------------------------------------------------------------------
+# Muon updates
+# ---------------------------------------------------------------------------------------
 def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, step, param_idx, seeder):
     """Per-parameter Muon step (``_triton_muon_step``, triton_muon_sr.py:116-120)."""
     if p.ndim < 2:
@@ -94,32 +114,6 @@ def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, s
     K.muon_apply([(p, out, K.ns_scale(p.shape), seeder(step, param_idx, 1))], lr, weight_decay)
 
 
-def muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
-                    seeder, owner=None, share=None, segments=None):
-    """Batched step over shape stacks (``_triton_muon_batch_step``, triton_muon_sr.py:128-177).
-
-    Prepare runs once per stack with seed S(step, shape_idx, 0) and counters running over the
-    whole stack; Newton-Schulz runs on chunks of the stack; apply uses
-    S(step, shape_idx * 10000 + i, 1). A stack where only some parameters have gradients
-    falls back to per-parameter steps with param_idx = shape_idx * 10000 + i.
-    ``owner(shape_idx, i) -> bool`` restricts the work to this rank's matrices; seeds and
-    counters stay global, so results do not depend on the number of ranks. ``share(params)``
-    is called after each stack (and, with ``segments``, after each segment of a stack) so its
-    weights can travel while the rest computes.
-    """
-    stacks = list(enumerate(shape_groups.items()))
-    if share is not None and not seeder.random:
-        # Largest stacks first, so that the stack whose weights are still in flight when the
-        # step ends is the smallest. Seeds keep each stack's own index, so the bits do not
-        # depend on this order (seeds drawn from torch's generator do: those keep the order).
-        stacks.sort(key=lambda e: -len(e[1][1]) * K.numel_of(e[1][0]))
-    for shape_idx, (shape, grp) in stacks:
-        _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay,
-                    step, seeder, owner, share, segments)
-        if share is not None:
-            share(grp)
-
-
 def _segments(n, count):
     """Split range(n) into ``count`` consecutive index ranges of near-equal length."""
     count = max(1, min(n, count))
@@ -127,68 +121,155 @@ def _segments(n, count):
     return [range(bounds[s], bounds[s + 1]) for s in range(count)]
 
 
-def _stack_step(shape_idx, shape, grp, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, weight_decay, step,
-                seeder, owner, share=None, segments=None):
-    """One shape stack of ``muon_batch_step``. With ``segments(shape, n) -> count`` the
-    stack's global index range is cut into that many consecutive segments; each rank runs
-    its own matrices segment by segment and ``share`` is called after every segment (on
-    every rank, also when it owned none of it), so the weights start travelling while the
-    rest of the stack computes. Chunks never span segments; the bits are those of the
-    unsegmented step."""
-    active = [p for p in grp if p.grad is not None]
-    if not active:
+class _Work:
+    """Where a batched step may do its work: ``owner(stack_idx, row) -> bool`` (None = all),
+    ``share(params)`` after each stack / segment and ``segments(shape, n)`` (None = whole
+    stacks), all from a ``sharding.Sharder``."""
+
+    def __init__(self, owner=None, share=None, segments=None):
+        self.owner, self.share, self.segments = owner, share, segments
+
+    def mine(self, stack_idx, row):
+        return self.owner is None or self.owner(stack_idx, row)
+
+
+def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work=None):
+    """Batched step over the shape stacks (``_triton_muon_batch_step``,
+    triton_muon_sr.py:128-177).
+
+    For stack number s of ``stacks.by_shape`` (first-appearance order): prepare over the whole
+    stack with seed S(step, s, 0) and counters running over the stack; Newton-Schulz on chunks
+    of at most NS_CHUNK_NUMEL elements; apply of row r with S(step, s * 10000 + r, 1). A stack
+    where only some parameters have gradients falls back to per-parameter steps with
+    param_idx = s * 10000 + r. With ``work`` only this rank's rows are computed (seeds and
+    counters stay global, so results do not depend on the number of ranks) and the weights
+    are shared as they are finished."""
+    work = work or _Work()
+    order = list(enumerate(stacks.by_shape.items()))
+    if work.share is not None and not seeder.random:
+        # Largest stacks first, so that the stack whose weights are still in flight when the
+        # step ends is the smallest. Seeds keep each stack's own index, so the bits do not
+        # depend on this order (seeds drawn from torch's generator do: those keep the order).
+        order.sort(key=lambda e: -len(e[1][1]) * K.numel_of(e[1][0]))
+    for s, (shape, members) in order:
+        _stack_step(s, shape, members, stacks.tensor[shape], beta, nesterov, ns_steps, lr, weight_decay, step,
+                    seeder, work)
+        if work.share is not None:
+            work.share(members)
+
+
+def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work):
+    """One shape stack of ``muon_batch_step``. With ``work.segments`` the stack's rows are cut
+    into consecutive segments; each rank runs its own rows segment by segment and
+    ``work.share`` is called after every segment (on every rank, also when it owned none of
+    it), so the weights start travelling while the rest of the stack computes. Chunks never
+    span segments; the bits are those of the unsegmented step."""
+    if all(p.grad is None for p in members):
         return
-    stacked_buf = stacked_bufs[shape]
-    if len(active) < len(grp):
-        for p in active:
-            i = buf_indices[id(p)]
-            if owner is None or owner(shape_idx, i):
-                muon_single_step(p, _grad_of(p), stacked_buf[i], beta, nesterov, ns_steps, lr, weight_decay,
-                                 step, shape_idx * 10000 + i, seeder)
+    if any(p.grad is None for p in members):
+        for r, p in enumerate(members):
+            if p.grad is None:
+                continue
+            if work.mine(s, r):
+                muon_single_step(p, _grad_of(p), momentum[r], beta, nesterov, ns_steps, lr, weight_decay, step,
+                                 s * 10000 + r, seeder)
             else:
-                seeder.skip(step, shape_idx * 10000 + i, 0)
-                seeder.skip(step, shape_idx * 10000 + i, 1)
+                seeder.skip(step, s * 10000 + r, 0)
+                seeder.skip(step, s * 10000 + r, 1)
         return
-    mine = [i for i in range(len(grp)) if owner is None or owner(shape_idx, i)]
-    segs = _segments(len(grp), segments(shape, len(grp)) if (segments and share) else 1)
     if len(shape) < 2:
         raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
+    rows = [r for r in range(len(members)) if work.mine(s, r)]
+    parts = _segments(len(members), work.segments(shape, len(members)) if (work.segments and work.share) else 1)
     numel = K.numel_of(shape)
-    work = None
     # seeds in the single-GPU draw order: the stack's prepare seed, then one apply seed per
-    # matrix in index order (all of them on every rank)
-    prep_seed = seeder(step, shape_idx, 0)
-    apply_seeds = [seeder(step, shape_idx * 10000 + i, 1) for i in range(len(grp))]
-    if mine:
-        work = torch.empty(len(mine), *shape, dtype=torch.bfloat16, device=stacked_buf.device)
-        K.muon_prepare([(_grad_of(grp[i]), stacked_buf[i], work[j], i * numel, prep_seed)
-                        for j, i in enumerate(mine)], beta, nesterov)
-    k = max(1, NS_CHUNK_NUMEL // max(1, numel))
+    # row in row order (all of them on every rank)
+    prep_seed = seeder(step, s, 0)
+    apply_seed = [seeder(step, s * 10000 + r, 1) for r in range(len(members))]
+    upd = None
+    if rows:
+        upd = torch.empty((len(rows),) + tuple(shape), dtype=torch.bfloat16, device=momentum.device)
+        K.muon_prepare([(_grad_of(members[r]), momentum[r], upd[j], r * numel, prep_seed) for j, r in enumerate(rows)],
+                       beta, nesterov)
+    chunk = max(1, NS_CHUNK_NUMEL // max(1, numel))
     scale = K.ns_scale(shape)
-    pos = 0  # position in `mine` (and `work`) where the current segment starts
-    for seg in segs:
-        end = pos
-        while end < len(mine) and mine[end] in seg:
-            end += 1
-        for s in range(pos, end, k):
-            out = K.newton_schulz(work[s:min(s + k, end)], ns_steps)
-            K.muon_apply([(grp[mine[s + j]], out[j], scale, apply_seeds[mine[s + j]]) for j in range(out.shape[0])],
+    lo = 0  # first position in `rows` (and `upd`) of the current segment
+    for part in parts:
+        hi = lo
+        while hi < len(rows) and rows[hi] in part:
+            hi += 1
+        for c in range(lo, hi, chunk):
+            out = K.newton_schulz(upd[c:min(c + chunk, hi)], ns_steps)
+            K.muon_apply([(members[rows[c + j]], out[j], scale, apply_seed[rows[c + j]]) for j in range(out.shape[0])],
                          lr, weight_decay)
             del out
-        pos = end
-        if len(segs) > 1:
-            share([grp[i] for i in seg])
-    del work
+        lo = hi
+        if len(parts) > 1:
+            work.share([members[r] for r in part])
+    del upd
 
 
-def _check_params(params, name):
-    for p in params:
-        assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
-        if p.grad is not None and p.grad.is_sparse:
-            raise RuntimeError(f"{name} does not support sparse gradients")
+# ---------------------------------------------------------------------------------------
+# Optimizers
+# ---------------------------------------------------------------------------------------
+class _MuonBase(Optimizer):
+    """Shared machinery of the Muon classes: batched-group stacks, the global step, seeds
+    and the optional sharder."""
+
+    _random_seeds = False   # True: seeds from torch's generator (MuonSR classes)
+    _record_step = True     # False: no "step" in the Muon state (MuonSR classes)
+
+    def _setup(self, shard):
+        self._shard = shard
+        self._reset_batched()
+
+    def _reset_batched(self):
+        self._stacks = {}
+        self._clock = _GlobalStep()
+
+    def load_state_dict(self, state_dict):
+        # stacks and the global step are rebuilt from the loaded state on the next step
+        # (muon_sr/muon_sr.py:149-158)
+        super().load_state_dict(state_dict)
+        self._reset_batched()
+
+    def _run_muon_group(self, gi, group, batched, batched_groups, seeder):
+        name = type(self).__name__
+        beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
+        lr, wd = group["lr"], group["weight_decay"]
+        sh = self._shard
+        if batched:
+            if id(group) not in self._stacks:
+                self._stacks[id(group)] = _MomentumStacks(group["params"], self.state)
+            stacks = self._stacks[id(group)]
+            for p in group["params"]:
+                _validate(p, name)
+            step = self._clock.advance(self.state, batched_groups, group["params"]) if self._record_step else 0
+            work = _Work(sh.muon_owner(gi, stacks.by_shape), sh.share, sh.segments) if sh else None
+            muon_batch_step(stacks, beta, nesterov, ns_steps, lr, wd, step, seeder, work)
+            return
+        for i, p in enumerate(group["params"]):
+            _validate(p, name)
+            if p.grad is None:
+                continue
+            st = self.state[p]
+            if not st:
+                if self._record_step:
+                    st["step"] = 0
+                st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+            if self._record_step:
+                st["step"] += 1
+            step = st.get("step", 0)
+            if sh and not sh.owns(gi, i):
+                seeder.skip(step, i, 0)
+                seeder.skip(step, i, 1)
+                continue
+            muon_single_step(p, _grad_of(p), st["momentum_buffer"], beta, nesterov, ns_steps, lr, wd, step, i, seeder)
+        if sh:
+            sh.share(group["params"])
 
 
-class TritonMuonSR(_StackedBufsMixin, Optimizer):
+class TritonMuonSR(_MuonBase):
     r"""Muon for bf16 matrices with stochastic rounding (drop-in for muon_sr.TritonMuonSR,
     muon_sr/triton_muon_sr.py:180-255).
 
@@ -203,16 +284,11 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
         shard: optional ``sharding.Sharder`` spreading the matrices over ranks
     """
 
-    _random_seeds = False
-    _record_step = True
-
     def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95, nesterov=True, ns_steps=5, batch_ns=False,
                  shard=None):
-        defaults = dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
-                        batch_ns=batch_ns)
-        super().__init__(params, defaults)
-        self._batch_state = {}
-        self._shard = shard
+        super().__init__(params, dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov,
+                                      ns_steps=ns_steps, batch_ns=batch_ns))
+        self._setup(shard)
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -220,54 +296,12 @@ class TritonMuonSR(_StackedBufsMixin, Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        seeder = _Seeder(self._random_seeds)
-        name = type(self).__name__
         if self._shard:
             self._shard.bind(self)
+        seeder = _Seeder(self._random_seeds)
+        batched_groups = [g for g in self.param_groups if g["batch_ns"]]
         for gi, group in enumerate(self.param_groups):
-            lr, wd = group["lr"], group["weight_decay"]
-            beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
-            if group["batch_ns"]:
-                gid = id(group)
-                if gid not in self._batch_state:
-                    self._batch_state[gid] = _init_stacked_bufs(group["params"], group["params"][0].device, self.state)
-                shape_groups, stacked_bufs, buf_indices = self._batch_state[gid]
-                _check_params(group["params"], name)
-                step = 0
-                if self._record_step:
-                    if not hasattr(self, "_global_step"):
-                        self._global_step = _restore_global_step(
-                            self.state, [g for g in self.param_groups if g["batch_ns"]])
-                    self._global_step += 1
-                    step = self._global_step
-                    for p in group["params"]:
-                        self.state[p]["step"] = self._global_step
-                owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
-                muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd, step,
-                                seeder, owner, self._shard.share if self._shard else None,
-                                self._shard.segments if self._shard else None)
-            else:
-                for param_idx, p in enumerate(group["params"]):
-                    assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
-                    if p.grad is None:
-                        continue
-                    if p.grad.is_sparse:
-                        raise RuntimeError(f"{name} does not support sparse gradients")
-                    state = self.state[p]
-                    if len(state) == 0:
-                        if self._record_step:
-                            state["step"] = 0
-                        state["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
-                    if self._record_step:
-                        state["step"] += 1
-                    if self._shard and not self._shard.owns(gi, param_idx):
-                        seeder.skip(state.get("step", 0), param_idx, 0)
-                        seeder.skip(state.get("step", 0), param_idx, 1)
-                        continue
-                    muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
-                                     state.get("step", 0), param_idx, seeder)
-                if self._shard:
-                    self._shard.share(group["params"])
+            self._run_muon_group(gi, group, group["batch_ns"], batched_groups, seeder)
         if self._shard:
             self._shard.sync_params(self)
         return loss
@@ -281,7 +315,11 @@ class MuonSR(TritonMuonSR):
     _record_step = False
 
 
-class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
+_MUON_DEFAULTS = dict(lr=0.02, momentum=0.95, nesterov=True, ns_steps=5, weight_decay=0)
+_ADAM_DEFAULTS = dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0)
+
+
+class TritonMuonSRWithAuxAdam(_MuonBase):
     r"""Hybrid Muon + AdamW with stochastic rounding (drop-in for
     muon_sr.TritonMuonSRWithAuxAdam, muon_sr/triton_muon_sr.py:258-373).
 
@@ -291,27 +329,14 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
         shard: optional ``sharding.Sharder`` spreading the work over ranks
     """
 
-    _random_seeds = False
-    _record_muon_step = True
-
     def __init__(self, param_groups, batch_ns=False, shard=None):
         for group in param_groups:
             assert "use_muon" in group
-            if group["use_muon"]:
-                group.setdefault("lr", 0.02)
-                group.setdefault("momentum", 0.95)
-                group.setdefault("nesterov", True)
-                group.setdefault("ns_steps", 5)
-                group.setdefault("weight_decay", 0)
-            else:
-                group.setdefault("lr", 3e-4)
-                group.setdefault("betas", (0.9, 0.95))
-                group.setdefault("eps", 1e-10)
-                group.setdefault("weight_decay", 0)
+            for key, value in (_MUON_DEFAULTS if group["use_muon"] else _ADAM_DEFAULTS).items():
+                group.setdefault(key, value)
         self.batch_ns = batch_ns
-        self._batch_state = {}
-        self._shard = shard
         super().__init__(param_groups, {})
+        self._setup(shard)
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -319,96 +344,31 @@ class TritonMuonSRWithAuxAdam(_StackedBufsMixin, Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        sh = self._shard
+        if sh:
+            sh.bind(self)
         seeder = _Seeder(self._random_seeds)
-        name = type(self).__name__
-        if self._shard:
-            self._shard.bind(self)
-        offsets, total = [], 0
-        for group in self.param_groups:
-            offsets.append(total)
-            total += len(group["params"])
-        order = list(range(len(self.param_groups)))
-        if self._shard and not self._random_seeds:
-            # AdamW groups (embedding, head) first so their broadcasts overlap the Muon work;
+        groups = self.param_groups
+        offsets = [sum(len(g["params"]) for g in groups[:gi]) for gi in range(len(groups))]
+        muon_groups = [g for g in groups if g["use_muon"]]
+        order = range(len(groups))
+        if sh and not self._random_seeds:
+            # AdamW groups (embedding, head) first so their transfers overlap the Muon work;
             # every group's math is independent of the processing order (seeds drawn from
             # torch's generator are not: those classes keep the order).
-            order.sort(key=lambda gi: bool(self.param_groups[gi]["use_muon"]))
+            order = sorted(order, key=lambda gi: bool(groups[gi]["use_muon"]))
         for gi in order:
-            group = self.param_groups[gi]
-            group_offset = offsets[gi]
+            group = groups[gi]
             if group["use_muon"]:
-                lr, wd = group["lr"], group["weight_decay"]
-                beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
-                if not group["params"]:
-                    continue
-                if self.batch_ns:
-                    gid = id(group)
-                    if gid not in self._batch_state:
-                        self._batch_state[gid] = _init_stacked_bufs(group["params"], group["params"][0].device,
-                                                                     self.state)
-                    shape_groups, stacked_bufs, buf_indices = self._batch_state[gid]
-                    _check_params(group["params"], name)
-                    step = 0
-                    if self._record_muon_step:
-                        if not hasattr(self, "_global_step"):
-                            self._global_step = _restore_global_step(
-                                self.state, [g for g in self.param_groups if g["use_muon"]])
-                        self._global_step += 1
-                        step = self._global_step
-                        for p in group["params"]:
-                            self.state[p]["step"] = self._global_step
-                    owner = self._shard.muon_owner(gi, shape_groups) if self._shard else None
-                    muon_batch_step(shape_groups, stacked_bufs, buf_indices, beta, nesterov, ns_steps, lr, wd,
-                                    step, seeder, owner, self._shard.share if self._shard else None,
-                                    self._shard.segments if self._shard else None)
-                else:
-                    for param_idx, p in enumerate(group["params"]):
-                        assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
-                        if p.grad is None:
-                            continue
-                        if p.grad.is_sparse:
-                            raise RuntimeError(f"{name} does not support sparse gradients")
-                        state = self.state[p]
-                        if len(state) == 0:
-                            if self._record_muon_step:
-                                state["step"] = 0
-                            state["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
-                        if self._record_muon_step:
-                            state["step"] += 1
-                        if self._shard and not self._shard.owns(gi, param_idx):
-                            seeder.skip(state.get("step", 0), param_idx, 0)
-                            seeder.skip(state.get("step", 0), param_idx, 1)
-                            continue
-                        muon_single_step(p, _grad_of(p), state["momentum_buffer"], beta, nesterov, ns_steps, lr, wd,
-                                         state.get("step", 0), param_idx, seeder)
-                    if self._shard:
-                        self._shard.share(group["params"])
-            else:
-                lr = group["lr"]
-                beta1, beta2 = group["betas"]
-                eps, wd = group["eps"], group["weight_decay"]
-                items = []
-                for i, p in enumerate(group["params"]):
-                    assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
-                    if p.grad is None:
-                        continue
-                    if p.grad.is_sparse:
-                        raise RuntimeError(f"{name} does not support sparse gradients")
-                    state = self.state[p]
-                    if len(state) == 0:
-                        state["step"] = 0
-                        state["ema"] = torch.zeros_like(p, dtype=torch.bfloat16)
-                        state["ema_squared"] = torch.zeros_like(p, dtype=torch.bfloat16)
-                    state["step"] += 1
-                    seed = seeder(state["step"], group_offset + i, 0)
-                    if self._shard and not self._shard.owns(gi, i):
-                        continue
-                    items.append((p, _grad_of(p), state["ema"], state["ema_squared"], state["step"], seed))
-                K.adamw_sr(items, lr, beta1, beta2, eps, wd)
-                if self._shard:
-                    self._shard.share(group["params"])
-        if self._shard:
-            self._shard.sync_params(self)
+                if group["params"]:
+                    self._run_muon_group(gi, group, self.batch_ns, muon_groups, seeder)
+                continue
+            adamw_group_step(self.state, group, offsets[gi], lambda step, idx: seeder(step, idx, 0),
+                             owns=(lambda i, gi=gi: sh.owns(gi, i)) if sh else None)
+            if sh:
+                sh.share(group["params"])
+        if sh:
+            sh.sync_params(self)
         return loss
 
 
@@ -417,4 +377,4 @@ class MuonSRWithAuxAdam(TritonMuonSRWithAuxAdam):
     arguments and state keys; SR noise seeded from torch's default generator."""
 
     _random_seeds = True
-    _record_muon_step = False
+    _record_step = False

@@ -54,7 +54,7 @@ def test_hybrid_requires_use_muon_and_fills_defaults():
 
 @pytest.mark.parametrize("kw,msg", [
     (dict(lr=-1.0), "lr must be"), (dict(eps=0.0), "eps must be positive"), (dict(betas=(0.9, 1.0)), "betas"),
-    (dict(block_size=48), "block_size"), (dict(optim_bits=32), "optim_bits"), (dict(min_8bit_size=-1), "optim_bits"),
+    (dict(block_size=48), "block_size"), (dict(optim_bits=32), "optim_bits"), (dict(min_8bit_size=-1), "min_8bit_size"),
 ])
 def test_adamw8bit_validation(kw, msg):
     p = torch.nn.Parameter(torch.zeros(4, dtype=torch.bfloat16))
