@@ -272,6 +272,38 @@ def run_ours(args, rank, world, local_rank):
     del opt8
     torch.cuda.empty_cache()
 
+    # ---- SR gradient accumulation (one micro-batch into every tensor through the
+    # accumulator hook, after the first) and configs[1]: TritonAdamW on the GPT-2 AdamW set ----
+    extra = {}
+    if rank == 0:
+        from muon_sr_b200 import TritonAdamW, TritonSRAccumulator
+        grads = [p.grad for p in params]
+
+        def micro_batch():
+            for p, g in zip(params, grads):
+                p.grad = g
+                TritonSRAccumulator._accum_hook(p)
+
+        micro_batch()  # first micro-batch creates the buffers
+        acc_ms = time_steps(micro_batch, 3, 1, 1)
+        for p, g in zip(params, grads):
+            del p.acc_grad
+            p.grad = g
+        gg = torch.Generator(device=device).manual_seed(1)
+        gpt2 = [torch.nn.Parameter(torch.empty(s, dtype=torch.bfloat16, device=device).normal_(0, 0.02, generator=gg))
+                for s in [(50257, 768)] + [(768,)] * 24]
+        for p in gpt2:
+            p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gg)
+        opt_a = TritonAdamW(gpt2, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01)
+        aw_ms = time_steps(opt_a.step, 50, 5, 1)
+        n_gpt2 = sum(p.numel() for p in gpt2)
+        extra = {"sr_accum_ms_per_microbatch": acc_ms,
+                 "sr_accum_hbm_gbs": 6 * n_all / (acc_ms * 1e-3) / 1e9,
+                 "adamw_sr_gpt2_ms": aw_ms,
+                 "adamw_sr_gpt2_hbm_gbs": 14 * n_gpt2 / (aw_ms * 1e-3) / 1e9}
+        del opt_a, gpt2
+        torch.cuda.empty_cache()
+
     # ---- end to end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
@@ -316,6 +348,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline_8bit": {"bound": "hbm", "kernel": "adamw8bit_kernel", "achieved": a8_gbs, "peak": hbm_gbs,
                               "unit": "GB/s", "frac": (a8_gbs / hbm_gbs) if a8_gbs else None,
                               "algorithmic_bytes": a8_bytes, "traffic": None},
+            "other_configs": extra,
             "gpu_launches": int(launches),
             "clocks": clocks,
             "e2e": e2e,
