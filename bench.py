@@ -36,6 +36,9 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 METRIC = "Llama-3-8B hybrid optimizer step ms; NS TFLOP/s; 8-bit AdamW HBM GB/s"
+# dram__bytes_read.sum + dram__bytes_write.sum of one adamw8bit_kernel launch on 2^28 elements
+# (block 256), from the capture summarised in profiles/adamw8bit_kernel_256M.md
+A8_DRAM_BYTES_PER_ELEMENT = (1.619793e9 + 1.024948e9) / (1 << 28)
 N_LAYERS, D, KV, FF, VOCAB = 32, 4096, 1024, 14336, 128256
 
 
@@ -344,10 +347,15 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (Newton-Schulz chain)",
                          "achieved": ns_tflops, "peak": peak_ns, "unit": "TFLOP/s",
                          "frac": (ns_tflops / peak_ns) if ns_tflops else None,
-                         "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None},
+                         "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None,
+                         "traffic_note": "tensor-bound chain of mixed shapes; per-launch DRAM bytes equal the "
+                                         "algorithmic operand bytes (profiles/gemm_pair_kernel_ns_4x4096.md)"},
             "roofline_8bit": {"bound": "hbm", "kernel": "adamw8bit_kernel", "achieved": a8_gbs, "peak": hbm_gbs,
                               "unit": "GB/s", "frac": (a8_gbs / hbm_gbs) if a8_gbs else None,
-                              "algorithmic_bytes": a8_bytes, "traffic": None},
+                              "algorithmic_bytes": a8_bytes,
+                              "traffic": A8_DRAM_BYTES_PER_ELEMENT * n_all,
+                              "traffic_note": "DRAM bytes per element of a 2^28-element ncu capture "
+                                              "(profiles/adamw8bit_kernel_256M.md) scaled to this step's elements"},
             "other_configs": extra,
             "gpu_launches": int(launches),
             "clocks": clocks,
