@@ -269,8 +269,10 @@ def run_ours(args, rank, world, local_rank):
     if shard is not None:
         owned = sum(p.numel() for p in params if shard._owner[id(p)] == shard.rank)
         a8_bytes_rank = owned * 10 + 16 * owned / 256
+        a8_elems_rank = owned
     else:
         a8_bytes_rank = a8_bytes
+        a8_elems_rank = n_all
     a8_gbs = a8_bytes_rank / (a8_kernel_ms * 1e-3) / 1e9 if a8_kernel_ms > 0 else None
     del opt8
     torch.cuda.empty_cache()
@@ -353,9 +355,10 @@ def run_ours(args, rank, world, local_rank):
             "roofline_8bit": {"bound": "hbm", "kernel": "adamw8bit_kernel", "achieved": a8_gbs, "peak": hbm_gbs,
                               "unit": "GB/s", "frac": (a8_gbs / hbm_gbs) if a8_gbs else None,
                               "algorithmic_bytes": a8_bytes,
-                              "traffic": A8_DRAM_BYTES_PER_ELEMENT * n_all,
+                              "traffic": A8_DRAM_BYTES_PER_ELEMENT * a8_elems_rank,
                               "traffic_note": "DRAM bytes per element of a 2^28-element ncu capture "
-                                              "(profiles/adamw8bit_kernel_256M.md) scaled to this step's elements"},
+                                              "(profiles/adamw8bit_kernel_256M.md) scaled to the elements "
+                                              "this rank updates per step, like achieved"},
             "other_configs": extra,
             "gpu_launches": int(launches),
             "clocks": clocks,
