@@ -4,7 +4,6 @@ import ctypes
 import os
 import re
 
-import pytest
 
 from muon_sr_b200 import _lib
 

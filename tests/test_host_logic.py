@@ -9,7 +9,6 @@ import torch.multiprocessing as mp
 
 from muon_sr_b200 import TritonAdamW8bit, TritonMuonSRWithAuxAdam, create_dynamic_map, seeds
 from muon_sr_b200.sharding import Sharder
-from oracle import adamw8bit as o8
 from oracle import philox as op
 from tests._golden import load
 
@@ -207,3 +206,34 @@ def test_sharded_state_gather_and_grad_reduce_two_ranks_gloo():
         assert ok_all and ok_dst and ok_red, (rank, ok_all, ok_dst, ok_red)
         assert keys[:5] == [["momentum_buffer", "step"]] * 5
         assert keys[5:] == [["ema", "ema_squared", "step"]] * 3
+
+
+def test_segments_cover_each_stack_in_order():
+    """A shape stack is shared in consecutive, non-empty, ordered segments that cover every
+    row exactly once, whatever count is asked for."""
+    from muon_sr_b200.muon import _segments
+    for n in (1, 2, 7, 64):
+        for count in (0, 1, 3, 8, 100):
+            segs = _segments(n, count)
+            rows = [r for s in segs for r in s]
+            assert rows == list(range(n))
+            assert all(len(s) > 0 for s in segs)
+            assert len(segs) == max(1, min(n, count))
+
+
+def test_sharder_segment_counts():
+    """About 4 ms of per-rank Newton-Schulz per segment, at least two matrices per rank per
+    segment, at most 8 segments; small stacks stay whole."""
+    class Fake(Sharder):
+        def __init__(self, world):  # no process group needed for the arithmetic
+            self.world = world
+    expect = {2: {(4096, 4096): 8, (1024, 4096): 1, (14336, 4096): 8, (4096, 14336): 8},
+              8: {(4096, 4096): 3, (1024, 4096): 1, (14336, 4096): 4, (4096, 14336): 2}}
+    counts = {(4096, 4096): 64, (1024, 4096): 64, (14336, 4096): 64, (4096, 14336): 32}
+    for world, table in expect.items():
+        sh = Fake(world)
+        for shape, want in table.items():
+            n = counts[shape]
+            got = sh.segments(shape, n)
+            assert got == want, (world, shape, got)
+            assert got == 1 or n // got >= 2 * world

@@ -7,7 +7,6 @@
 * Newton-Schulz: against the reference's own ``_newton_schulz`` outputs (golden, CPU) and
   against the same torch ops run on this GPU, north-star tolerance rel. Frobenius <= 1e-2.
 """
-import numpy as np
 import pytest
 import torch
 

@@ -1,11 +1,10 @@
 """The CPU oracle against the golden vectors produced by the reference itself."""
 import numpy as np
 import pytest
-import torch
 
 from oracle import adamw8bit as o8
 from oracle import elementwise as ew
-from oracle.newton_schulz import newton_schulz, rel_frobenius
+from oracle.newton_schulz import newton_schulz
 from oracle.philox import deterministic_seed, philox_randint, triton_key
 from oracle.sr import rne_bf16, truncate_bf16
 from tests._golden import assert_bits_equal, bits_of, load, to_bf16
