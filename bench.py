@@ -250,6 +250,33 @@ def run_ours(args, rank, world, local_rank):
         per_rank = [None] * world
         dist.all_gather_object(per_rank, breakdown)
 
+    # elementwise kernels' algorithmic HBM rate (this rank's tensors)
+    if shard is None:
+        own_muon, own_adam = n_muon, n_adam
+    else:
+        own_muon = sum(p.numel() for p in muon if shard._owner[id(p)] == shard.rank)
+        own_adam = sum(p.numel() for p in adam if shard._owner[id(p)] == shard.rank)
+
+    def ew_rates(bd):
+        out = {}
+        for name, nbytes in (("muon_prepare", 8 * own_muon), ("muon_apply", 6 * own_muon), ("adamw_sr", 14 * own_adam)):
+            if bd.get(name, 0) > 0 and nbytes:
+                out[name] = nbytes / (bd[name] * 1e-3) / 1e9
+        return out
+
+    # ---- the same step with the opt-in fast noise stream (not the reference's bits) ----
+    K.set_sr_noise("fast")
+    timers.events.clear()
+    timers.enabled = True
+    fast_ms = time_steps(opt.step, args.steps, 1, world)
+    timers.enabled = False
+    fast_bd = {k: v / (args.steps + 1) for k, v in timers.totals_ms().items()}
+    K.set_sr_noise("reference")
+    fast_noise = {"value": fast_ms, "unit": "ms", "breakdown_ms_per_step": fast_bd,
+                  "elementwise_hbm_gbs": ew_rates(fast_bd),
+                  "note": "set_sr_noise('fast'): one Philox4x32-10 call per 8 rounded values; unbiased SR, "
+                          "different bits than the reference; not the headline"}
+
     # ---- 8-bit blockwise AdamW on the same tensors ----
     params = muon + adam
     opt8 = TritonAdamW8bit([dict(params=params, optim_bits=8)], lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
@@ -345,6 +372,8 @@ def run_ours(args, rank, world, local_rank):
             "ns_tflops": ns_tflops, "ns_tflop_per_step": total_flops / 1e12,
             "adamw8bit_hbm_gbs": a8_gbs, "adamw8bit_step_ms": a8_step_ms, "adamw8bit_kernel_ms": a8_kernel_ms,
             "breakdown_ms_per_step": breakdown,
+            "elementwise_hbm_gbs": ew_rates(breakdown),
+            "fast_noise": fast_noise,
             "breakdown_ms_per_step_per_rank": per_rank if world > 1 else None,
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (Newton-Schulz chain)",
                          "achieved": ns_tflops, "peak": peak_ns, "unit": "TFLOP/s",

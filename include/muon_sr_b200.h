@@ -37,6 +37,18 @@ enum msr_status {
 
 /* Version of this ABI (bumped on any signature change). */
 int msr_abi_version(void);
+
+/* Stochastic-rounding noise stream of every rounding kernel (process-wide; no counterpart
+ * in the reference):
+ *   MSR_SR_NOISE_REFERENCE (default) -- word 0 of Philox4x32-10 at the element offset
+ *     truncated to 32 bits, one generator call per rounded value: the reference's bits.
+ *   MSR_SR_NOISE_FAST -- one Philox4x32-10 call per 8 consecutive elements: element counter
+ *     c uses 16-bit half (c & 1) of output word ((c >> 1) & 3) at counter (c >> 3), same
+ *     keys. Each value is still rounded up with probability equal to its fractional part
+ *     (unbiased stochastic rounding), but the bits differ from the reference's.
+ * Returns MSR_ERR_INVALID for an unknown mode. */
+enum msr_sr_noise { MSR_SR_NOISE_REFERENCE = 0, MSR_SR_NOISE_FAST = 1 };
+int msr_set_sr_noise(int mode);
 /* Static description of a status code. */
 const char* msr_status_string(int status);
 /* Detail message of the last failing call on the calling host thread ("" if none). */

@@ -10,6 +10,7 @@ from ._version import __version__
 from .adamw import SRAccumulator, TritonAdamW, TritonSRAccumulator
 from .adamw8bit import TritonAdamW8bit, create_dynamic_map
 from .muon import MuonSR, MuonSRWithAuxAdam, TritonMuonSR, TritonMuonSRWithAuxAdam
+from .kernels import set_sr_noise
 from .sharding import Sharder
 
 __all__ = [
@@ -18,5 +19,5 @@ __all__ = [
     "TritonAdamW", "TritonSRAccumulator",
     "MuonSR", "MuonSRWithAuxAdam",
     "TritonMuonSR", "TritonMuonSRWithAuxAdam",
-    "Sharder", "create_dynamic_map",
+    "Sharder", "create_dynamic_map", "set_sr_noise",
 ]

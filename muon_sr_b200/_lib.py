@@ -56,6 +56,7 @@ class Adam8Hparams(ctypes.Structure):
 # (name, restype, argtypes) of every exported symbol, in header order.
 SIGNATURES = [
     ("msr_abi_version", c_int, []),
+    ("msr_set_sr_noise", c_int, [c_int]),
     ("msr_status_string", ctypes.c_char_p, [c_int]),
     ("msr_last_error", ctypes.c_char_p, []),
     ("msr_device_error", c_int, [c_void_p, c_int]),

@@ -123,7 +123,7 @@ __device__ __forceinline__ float group_max(float v, float* red) {
 constexpr size_t smem_for(bool tables) { return 2 * 256 * 4 + (tables ? MSR_QT_BYTES : 0); }
 
 // EPT elements per thread, BS elements per quantisation block.
-template <int BS, bool TABLES>
+template <int BS, bool TABLES, bool FAST>
 __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
   constexpr int EPT = BS > 2048 ? 16 : 8;
   constexpr int TILE = Q_THREADS * EPT;
@@ -158,7 +158,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
     uint16_t* P = static_cast<uint16_t*>(E.param);
     const uint16_t* Gp = static_cast<const uint16_t*>(E.grad);
     const bool vec = a.vec[ei] && base + EPT <= n;
-    const PhiloxKey kp = make_key(E.key_p);
+    const SrNoise<FAST> np_{make_key(E.key_p)};
 
     uint16_t pb[EPT], gb[EPT];
     if (vec) {
@@ -232,6 +232,11 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
     }
 
     // Adam update (decay after the step, bitsandbytes order) -- :72-80
+    uint32_t rp[EPT];
+    if (FAST) {
+#pragma unroll
+      for (int h = 0; h < EPT; h += 8) np_.eight(static_cast<uint64_t>(base + h), rp + h);
+    }
     float mmax = 0.f, vmax = 0.f;
 #pragma unroll
     for (int j = 0; j < EPT; ++j) {
@@ -242,7 +247,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
       const float p = bf16_bits_to_f32(pb[j]);
       const float upd = fsub(p, __fdiv_rn(fmul(E.coef, m[j]), fadd(__fsqrt_rn(v[j]), E.sqrt_bc2_eps)));
       const float updated = fmul(upd, hp.decay);
-      if (fin) pb[j] = sr_bf16_bits(updated, philox_word0(static_cast<uint32_t>(base + j), kp));
+      if (fin) pb[j] = sr_bf16_bits(updated, FAST ? rp[j] : np_.at(static_cast<uint64_t>(base + j)));
       if (base + j < n) {
         mmax = fmaxf(mmax, fabsf(m[j]));
         vmax = fmaxf(vmax, fabsf(v[j]));
@@ -308,15 +313,23 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
         E.absmax2[base / BS] = vmax;
       }
     } else {
-      const PhiloxKey km = make_key(E.key_m), kv = make_key(E.key_v);
+      const SrNoise<FAST> nm{make_key(E.key_m)}, nv{make_key(E.key_v)};
       uint16_t* S1 = static_cast<uint16_t*>(E.state1);
       uint16_t* S2 = static_cast<uint16_t*>(E.state2);
       uint16_t mb[EPT], vb[EPT];
+      uint32_t rm[EPT], rv[EPT];
+      if (FAST) {
+#pragma unroll
+        for (int h = 0; h < EPT; h += 8) {
+          nm.eight(static_cast<uint64_t>(base + h), rm + h);
+          nv.eight(static_cast<uint64_t>(base + h), rv + h);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < EPT; ++j) {
-        const uint32_t ctr = static_cast<uint32_t>(base + j);
-        mb[j] = sr_bf16_bits(m[j], philox_word0(ctr, km));
-        vb[j] = sr_bf16_bits(v[j], philox_word0(ctr, kv));
+        const uint64_t ctr = static_cast<uint64_t>(base + j);
+        mb[j] = sr_bf16_bits(m[j], FAST ? rm[j] : nm.at(ctr));
+        vb[j] = sr_bf16_bits(v[j], FAST ? rv[j] : nv.at(ctr));
       }
       if (vec) {
 #pragma unroll
@@ -336,23 +349,25 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
   }
 }
 
-template <int BS, bool TABLES>
+template <int BS, bool TABLES, bool FAST>
 int launch_variant(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
   const int64_t cap = static_cast<int64_t>(sm_count()) * Q_BLOCKS_PER_SM;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
   constexpr size_t smem = smem_for(TABLES);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
-  adamw8bit_kernel<BS, TABLES><<<grid, Q_THREADS, smem, s>>>(a);
+  adamw8bit_kernel<BS, TABLES, FAST><<<grid, Q_THREADS, smem, s>>>(a);
   return check_launch("adamw8bit_kernel");
 }
 
 template <int BS>
 int launch_bs(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
-  return a.hp.qtables ? launch_variant<BS, true>(a, tiles, s) : launch_variant<BS, false>(a, tiles, s);
+  if (sr_noise_fast())
+    return a.hp.qtables ? launch_variant<BS, true, true>(a, tiles, s) : launch_variant<BS, false, true>(a, tiles, s);
+  return a.hp.qtables ? launch_variant<BS, true, false>(a, tiles, s) : launch_variant<BS, false, false>(a, tiles, s);
 }
 
 inline bool al(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

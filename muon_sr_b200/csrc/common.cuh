@@ -58,6 +58,74 @@ __device__ __forceinline__ uint32_t philox_word0(uint32_t ctr, PhiloxKey key) {
   return c0;
 }
 
+// All four Philox4x32-10 output words for the 64-bit counter (ctr_lo32, ctr_hi32, 0, 0).
+__device__ __forceinline__ uint4 philox4(uint64_t ctr, PhiloxKey key) {
+  uint32_t c0 = static_cast<uint32_t>(ctr), c1 = static_cast<uint32_t>(ctr >> 32), c2 = 0u, c3 = 0u;
+  uint32_t k0 = key.k0, k1 = key.k1;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo0 = 0xD2511F53u * c0;
+    const uint32_t hi2 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t lo2 = 0xCD9E8D57u * c2;
+    const uint32_t n0 = hi2 ^ c1 ^ k0;
+    const uint32_t n2 = hi0 ^ c3 ^ k1;
+    c1 = lo2;
+    c3 = lo0;
+    c0 = n0;
+    c2 = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return make_uint4(c0, c1, c2, c3);
+}
+
+// ---------------------------------------------------------------------------------------
+// Stochastic-rounding noise streams (the low 16 bits of each value are used)
+//  * SrNoise<false> -- the reference's: word 0 of Philox4x32-10 at the counter truncated to
+//    32 bits, one generator call per rounded value (bit-identical to muon_sr).
+//  * SrNoise<true>  -- fast mode (msr_set_sr_noise): one generator call per 8 consecutive
+//    counters; counter c uses the 16-bit half (c & 1) of word ((c >> 1) & 3) of Philox4x32-10
+//    at counter (c >> 3) (64-bit). Same keys. Statistically an unbiased 16-bit uniform per
+//    value like the reference's, but different bits.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t half_of(uint4 w, uint32_t k) {
+  const uint32_t word = k < 2 ? w.x : (k < 4 ? w.y : (k < 6 ? w.z : w.w));
+  return (word >> (16u * (k & 1u))) & 0xFFFFu;
+}
+
+template <bool FAST>
+struct SrNoise {
+  PhiloxKey key;
+
+  __device__ __forceinline__ uint32_t at(uint64_t ctr) const {
+    if (FAST) return half_of(philox4(ctr >> 3, key), static_cast<uint32_t>(ctr & 7u));
+    return philox_word0(static_cast<uint32_t>(ctr), key);
+  }
+
+  // Noise for the 8 consecutive counters ctr0 .. ctr0 + 7 into r[0..7].
+  __device__ __forceinline__ void eight(uint64_t ctr0, uint32_t* r) const {
+    if (!FAST) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = philox_word0(static_cast<uint32_t>(ctr0 + j), key);
+      return;
+    }
+    const uint4 w0 = philox4(ctr0 >> 3, key);
+    const uint32_t off = static_cast<uint32_t>(ctr0 & 7u);
+    if (off == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = half_of(w0, j);
+      return;
+    }
+    const uint4 w1 = philox4((ctr0 >> 3) + 1, key);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t k = off + j;
+      r[j] = k < 8 ? half_of(w0, k) : half_of(w1, k - 8);
+    }
+  }
+};
+
 // ---------------------------------------------------------------------------------------
 // Rounding
 // ---------------------------------------------------------------------------------------

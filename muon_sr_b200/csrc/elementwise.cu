@@ -45,9 +45,9 @@ __global__ void philox_fill_kernel(uint32_t* out, int64_t n, uint64_t ctr_base, 
 // ---------------------------------------------------------------------------------------
 // SR gradient accumulation: acc <- SR(acc + g) -- muon_sr/triton_adamw.py:206-229
 // ---------------------------------------------------------------------------------------
-__device__ __forceinline__ uint16_t accum_one(uint16_t a, uint16_t g, uint32_t ctr, PhiloxKey key) {
+__device__ __forceinline__ uint16_t accum_one(uint16_t a, uint16_t g, uint32_t rnd) {
   const float s = fadd(bf16_bits_to_f32(a), bf16_bits_to_f32(g));
-  return sr_bf16_bits(s, philox_word0(ctr, key));
+  return sr_bf16_bits(s, rnd);
 }
 
 // First micro-batch: SR(0 + g) == g exactly (g is already bf16), except -0 + 0 = +0.
@@ -68,10 +68,11 @@ __global__ __launch_bounds__(EW_THREADS) void grad_accum_first_kernel(uint16_t* 
     acc[i] = first_one(g[i]);
 }
 
-template <bool VEC>
+template <bool VEC, bool FAST>
 __global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __restrict__ acc,
                                                                const uint16_t* __restrict__ g,
                                                                int64_t n, PhiloxKey key) {
+  const SrNoise<FAST> nz{key};
   const int64_t nchunks = (n + EW_CHUNK - 1) / EW_CHUNK;
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
     const int64_t base = chunk * EW_CHUNK;
@@ -90,18 +91,20 @@ __global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __r
         const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
         if (idx + EW_VEC <= n) {
           U16x8 o;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            o.v[j] = accum_one(va[it].v[j], vg[it].v[j], static_cast<uint32_t>(idx + j), key);
+            o.v[j] = accum_one(va[it].v[j], vg[it].v[j], FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
           st_u16x8(acc + idx, o);
         } else {
-          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one(acc[i], g[i], static_cast<uint32_t>(i), key);
+          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
         }
       }
     } else {
       for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
-        if (i < n) acc[i] = accum_one(acc[i], g[i], static_cast<uint32_t>(i), key);
+        if (i < n) acc[i] = accum_one(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
       }
     }
   }
@@ -119,16 +122,20 @@ struct PrepareArgs {
   int nesterov;
 };
 
+// `rnd()` yields the element's noise word; it is called after the math, where the noise is
+// consumed, which keeps the register allocation of the Philox chain as short as possible.
+template <class Rnd>
 __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, float beta, float omb, bool nesterov,
-                                            uint32_t ctr, PhiloxKey key, uint16_t& buf_out, uint16_t& upd_out) {
+                                            Rnd rnd, uint16_t& buf_out, uint16_t& upd_out) {
   const float g = bf16_bits_to_f32(g_bits);
   const float buf = bf16_bits_to_f32(b_bits);
   const float nb = fadd(buf, fmul(omb, fsub(g, buf)));
   const float upd = nesterov ? fadd(g, fmul(beta, fsub(nb, g))) : nb;
-  buf_out = sr_bf16_bits(nb, philox_word0(ctr, key));
+  buf_out = sr_bf16_bits(nb, rnd());
   upd_out = rne_bf16_bits(upd);
 }
 
+template <bool FAST>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
   const int64_t total = a.prefix[a.count];
   const bool nesterov = a.nesterov != 0;
@@ -139,7 +146,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
     uint16_t* mb = static_cast<uint16_t*>(E.momentum);
     uint16_t* up = static_cast<uint16_t*>(E.update);
     const int64_t n = E.numel;
-    const PhiloxKey key = make_key(E.key);
+    const SrNoise<FAST> nz{make_key(E.key)};
     const uint64_t cb = E.ctr_base;
     const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
     if (a.vec[ei]) {
@@ -157,17 +164,18 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
         const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
         if (idx + EW_VEC <= n) {
           U16x8 ob, ou;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(cb + static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
             prepare_one(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
-                        static_cast<uint32_t>(cb + static_cast<uint64_t>(idx + j)), key, ob.v[j], ou.v[j]);
+                        [&] { return FAST ? r[j] : nz.at(cb + static_cast<uint64_t>(idx + j)); }, ob.v[j], ou.v[j]);
           st_u16x8(mb + idx, ob);
           st_u16x8(up + idx, ou);
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t ob, ou;
-            prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
-                        ob, ou);
+            prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
             mb[i] = ob;
             up[i] = ou;
           }
@@ -178,8 +186,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t ob, ou;
-          prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, static_cast<uint32_t>(cb + static_cast<uint64_t>(i)), key,
-                      ob, ou);
+          prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
           mb[i] = ob;
           up[i] = ou;
         }
@@ -200,13 +207,14 @@ struct ApplyArgs {
 };
 
 __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, float scale, float lr, float decay,
-                                              uint32_t ctr, PhiloxKey key) {
+                                              uint32_t rnd) {
   const float u = fmul(bf16_bits_to_f32(u_bits), scale);
   float p = fmul(bf16_bits_to_f32(p_bits), decay);
   p = fsub(p, fmul(lr, u));
-  return sr_bf16_bits(p, philox_word0(ctr, key));
+  return sr_bf16_bits(p, rnd);
 }
 
+template <bool FAST>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
@@ -215,7 +223,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* u = static_cast<const uint16_t*>(E.update);
     const int64_t n = E.numel;
-    const PhiloxKey key = make_key(E.key);
+    const SrNoise<FAST> nz{make_key(E.key)};
     const float scale = E.scale;
     const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
     if (a.vec[ei]) {
@@ -233,18 +241,22 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_
         const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
         if (idx + EW_VEC <= n) {
           U16x8 o;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            o.v[j] = apply_one(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay, static_cast<uint32_t>(idx + j), key);
+            o.v[j] = apply_one(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay,
+                               FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
           st_u16x8(p + idx, o);
         } else {
-          for (int64_t i = idx; i < n; ++i) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, static_cast<uint32_t>(i), key);
+          for (int64_t i = idx; i < n; ++i)
+            p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
         }
       }
     } else {
       for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
-        if (i < n) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, static_cast<uint32_t>(i), key);
+        if (i < n) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
       }
     }
   }
@@ -261,9 +273,9 @@ struct AdamWArgs {
   msr_adamw_hparams hp;
 };
 
+template <class Rnd>
 __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uint16_t& m_bits, uint16_t& v_bits,
-                                          const msr_adamw_hparams& hp, float step_size, float bc2s, uint32_t ctr,
-                                          PhiloxKey km, PhiloxKey kv, PhiloxKey kp) {
+                                          const msr_adamw_hparams& hp, float step_size, float bc2s, Rnd rnd) {
   const float g = bf16_bits_to_f32(g_bits);
   float m = bf16_bits_to_f32(m_bits);
   float v = bf16_bits_to_f32(v_bits);
@@ -273,13 +285,13 @@ __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uin
   const float denom = fadd(__fdiv_rn(__fsqrt_rn(v), bc2s), hp.eps);
   p = fmul(p, hp.decay);
   p = fsub(p, __fdiv_rn(fmul(step_size, m), denom));
-  m_bits = sr_bf16_bits(m, philox_word0(ctr, km));
-  v_bits = sr_bf16_bits(v, philox_word0(ctr, kv));
-  p_bits = sr_bf16_bits(p, philox_word0(ctr, kp));
+  m_bits = sr_bf16_bits(m, rnd(0));
+  v_bits = sr_bf16_bits(v, rnd(1));
+  p_bits = sr_bf16_bits(p, rnd(2));
 }
 
 // ITERS vectors of 8 elements per thread and chunk; MINB CTAs per SM for the register budget.
-template <int ITERS, int MINB>
+template <int ITERS, int MINB, bool FAST>
 __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
   constexpr int64_t CHUNK = EW_THREADS * EW_VEC * ITERS;
   const int64_t total = a.prefix[a.count];
@@ -291,7 +303,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
     uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
     uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
     const int64_t n = E.numel;
-    const PhiloxKey km = make_key(E.key_m), kv = make_key(E.key_v), kp = make_key(E.key_p);
+    const SrNoise<FAST> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
     const float ss = E.step_size, bc2s = E.bc2_sqrt;
     const int64_t base = (chunk - a.prefix[ei]) * CHUNK;
     if (a.vec[ei]) {
@@ -310,17 +322,29 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
       for (int it = 0; it < ITERS; ++it) {
         const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
         if (idx + EW_VEC <= n) {
+          uint32_t rm[EW_VEC], rv[EW_VEC], rp[EW_VEC];
+          if (FAST) {
+            nm.eight(static_cast<uint64_t>(idx), rm);
+            nv.eight(static_cast<uint64_t>(idx), rv);
+            np_.eight(static_cast<uint64_t>(idx), rp);
+          }
 #pragma unroll
-          for (int j = 0; j < EW_VEC; ++j)
-            adamw_one(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s,
-                      static_cast<uint32_t>(idx + j), km, kv, kp);
+          for (int j = 0; j < EW_VEC; ++j) {
+            const uint64_t c = static_cast<uint64_t>(idx + j);
+            adamw_one(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s, [&](int w) {
+              return w == 0 ? (FAST ? rm[j] : nm.at(c)) : w == 1 ? (FAST ? rv[j] : nv.at(c)) : (FAST ? rp[j] : np_.at(c));
+            });
+          }
           st_u16x8(p + idx, vp[it]);
           st_u16x8(m + idx, vm[it]);
           st_u16x8(v + idx, vv[it]);
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t pb = p[i], mb = m[i], vb = v[i];
-            adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, static_cast<uint32_t>(i), km, kv, kp);
+            adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+              const uint64_t c = static_cast<uint64_t>(i);
+              return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
+            });
             p[i] = pb; m[i] = mb; v[i] = vb;
           }
         }
@@ -330,7 +354,10 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t pb = p[i], mb = m[i], vb = v[i];
-          adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, static_cast<uint32_t>(i), km, kv, kp);
+          adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+              const uint64_t c = static_cast<uint64_t>(i);
+              return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
+            });
           p[i] = pb; m[i] = mb; v[i] = vb;
         }
       }
@@ -440,12 +467,10 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
           static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
     return check_launch("grad_accum_first_kernel");
   }
-  if (vec)
-    grad_accum_kernel<true><<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(
-        static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n, make_key(key));
-  else
-    grad_accum_kernel<false><<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(
-        static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n, make_key(key));
+  auto* kern = vec ? (sr_noise_fast() ? grad_accum_kernel<true, true> : grad_accum_kernel<true, false>)
+                  : (sr_noise_fast() ? grad_accum_kernel<false, true> : grad_accum_kernel<false, false>);
+  kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(static_cast<uint16_t*>(acc),
+                                                               static_cast<const uint16_t*>(grad), n, make_key(key));
   return check_launch("grad_accum_kernel");
 }
 
@@ -472,7 +497,8 @@ int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, fl
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    muon_prepare_kernel<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    auto* kern = sr_noise_fast() ? muon_prepare_kernel<true> : muon_prepare_kernel<false>;
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("muon_prepare_kernel");
     if (st) return st;
   }
@@ -499,7 +525,8 @@ int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float de
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    muon_apply_kernel<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    auto* kern = sr_noise_fast() ? muon_apply_kernel<true> : muon_apply_kernel<false>;
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("muon_apply_kernel");
     if (st) return st;
   }
@@ -527,7 +554,9 @@ int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    adamw_kernel<ADAMW_ITERS, ADAMW_MINB><<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    auto* kern = sr_noise_fast() ? adamw_kernel<ADAMW_ITERS, ADAMW_MINB, true>
+                                 : adamw_kernel<ADAMW_ITERS, ADAMW_MINB, false>;
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("adamw_kernel");
     if (st) return st;
   }

@@ -10,6 +10,9 @@ namespace msr {
 
 static thread_local char t_last_error[512] = "";
 static std::atomic<uint64_t> g_launches{0};
+static std::atomic<int> g_sr_noise{MSR_SR_NOISE_REFERENCE};
+
+bool sr_noise_fast() { return g_sr_noise.load(std::memory_order_relaxed) == MSR_SR_NOISE_FAST; }
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -52,6 +55,13 @@ int require_sm100() {
 extern "C" {
 
 int msr_abi_version(void) { return 1; }
+
+int msr_set_sr_noise(int mode) {
+  if (mode != MSR_SR_NOISE_REFERENCE && mode != MSR_SR_NOISE_FAST)
+    return msr::fail(MSR_ERR_INVALID, "msr_set_sr_noise: unknown mode %d", mode);
+  msr::g_sr_noise.store(mode);
+  return MSR_OK;
+}
 
 const char* msr_status_string(int status) {
   switch (status) {

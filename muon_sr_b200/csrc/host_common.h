@@ -23,4 +23,7 @@ int require_sm100();
 
 inline cudaStream_t to_stream(msr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Stochastic-rounding noise stream selected with msr_set_sr_noise (true: fast mode).
+bool sr_noise_fast();
+
 }  // namespace msr

@@ -9,7 +9,7 @@ the reference's own code run under the Triton interpreter.
 import numpy as np
 import torch
 
-from .philox import philox_randint, triton_key
+from .philox import sr_noise, triton_key
 from .sr import bf16_to_f32, sr_bf16
 
 f32 = np.float32
@@ -71,13 +71,14 @@ def adamw8bit_coefficients(lr, beta1, beta2, eps, weight_decay, step):
 
 
 def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2, eps,
-              weight_decay, step, seed, block, quantized):
+              weight_decay, step, seed, block, quantized, noise="reference"):
     """``_adamw_8bit_kernel`` -- ``triton_adamw_8bit.py:56-99``, all blocks of one tensor.
 
     Quantized path: s1/s2 are uint8 codes and absmax1/absmax2 fp32 per block. Otherwise
     s1/s2 are bf16 bits (SR with seed + 1 / seed + 2). BC1 = 1 - b1**step and
     BC2 = 1 - b2**step come from the host in double and are passed as fp32 (:203).
-    Returns (p, s1, s2, absmax1, absmax2) with the same dtypes as the inputs.
+    Returns (p, s1, s2, absmax1, absmax2) with the same dtypes as the inputs. ``noise``
+    selects the reference's noise stream or the engine's fast one.
     """
     n = p_bits.size
     bc1, bc2, lr32, b1, omb1, b2, omb2, eps32, decay = adamw8bit_coefficients(
@@ -100,8 +101,7 @@ def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2
         coef = f32(lr32 * sq_bc2 / bc1)
         upd = (p - coef * m / (np.sqrt(v) + sq_bc2 * eps32)).astype(f32)
         updated = (upd * decay).astype(f32)
-    ctr = np.arange(n, dtype=np.uint64)
-    rounded = sr_bf16(updated, philox_randint(triton_key(seed), ctr))
+    rounded = sr_bf16(updated, sr_noise(triton_key(seed), n, 0, noise))
     p_out = np.where(finite, rounded, p_bits.astype(np.uint16)).astype(np.uint16)
     if quantized:
         s1o = np.empty(n, np.uint8)
@@ -117,6 +117,6 @@ def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2
             a1[b] = mm
             a2[b] = vm
         return p_out, s1o, s2o, a1, a2
-    m_sr = sr_bf16(m, philox_randint(triton_key(seed, 1), ctr))
-    v_sr = sr_bf16(v, philox_randint(triton_key(seed, 2), ctr))
+    m_sr = sr_bf16(m, sr_noise(triton_key(seed, 1), n, 0, noise))
+    v_sr = sr_bf16(v, sr_noise(triton_key(seed, 2), n, 0, noise))
     return p_out, m_sr, v_sr, absmax1, absmax2

@@ -14,7 +14,7 @@ them in fp32 and can differ from this by one fp32 ulp in a coefficient.)
 """
 import numpy as np
 
-from .philox import philox_randint, triton_key
+from .philox import sr_noise, triton_key
 from .sr import bf16_to_f32, rne_bf16, sr_bf16
 
 f32 = np.float32
@@ -26,17 +26,18 @@ def counters(n: int, ctr_base: int = 0) -> np.ndarray:
     return (np.arange(n, dtype=np.uint64) + np.uint64(ctr_base)) & np.uint64(0xFFFFFFFF)
 
 
-def grad_accum(acc_bits, grad_bits, seed: int):
-    """``_grad_accum_kernel`` -- ``muon_sr/triton_adamw.py:206-229``: acc <- SR(acc + g)."""
+def grad_accum(acc_bits, grad_bits, seed: int, noise: str = "reference"):
+    """``_grad_accum_kernel`` -- ``muon_sr/triton_adamw.py:206-229``: acc <- SR(acc + g).
+    ``noise`` selects the reference's noise stream or the engine's fast one."""
     acc = bf16_to_f32(acc_bits)
     g = bf16_to_f32(grad_bits)
     s = (acc + g).astype(f32)
-    r = philox_randint(triton_key(seed), counters(acc.size))
+    r = sr_noise(triton_key(seed), acc.size, 0, noise)
     return sr_bf16(s, r)
 
 
 def muon_prepare(g_bits, buf_bits, beta: float, nesterov: bool, seed: int, ctr_base: int = 0,
-                 return_f32: bool = False):
+                 return_f32: bool = False, noise: str = "reference"):
     """``_muon_prepare_kernel`` -- ``muon_sr/triton_muon_sr.py:18-50``.
 
     new_buf = buf + (1 - beta) * (g - buf); update = g + beta * (new_buf - g) (Nesterov) or
@@ -57,7 +58,7 @@ def muon_prepare(g_bits, buf_bits, beta: float, nesterov: bool, seed: int, ctr_b
         update = (g + f32(beta) * (new_buf - g)).astype(f32)
     else:
         update = new_buf
-    r = philox_randint(triton_key(seed), counters(g.size, ctr_base))
+    r = sr_noise(triton_key(seed), g.size, ctr_base, noise)
     if return_f32:
         return sr_bf16(new_buf, r), rne_bf16(update), update
     return sr_bf16(new_buf, r), rne_bf16(update)
@@ -69,7 +70,7 @@ def ns_scale(rows: int, cols: int) -> float:
     return max(1.0, rows / cols) ** 0.5
 
 
-def muon_apply(p_bits, upd_bits, lr: float, weight_decay: float, scale: float, seed: int):
+def muon_apply(p_bits, upd_bits, lr: float, weight_decay: float, scale: float, seed: int, noise: str = "reference"):
     """``_muon_apply_kernel`` -- ``muon_sr/triton_muon_sr.py:53-80``:
     p <- SR(p * (1 - lr * wd) - lr * (update * scale))."""
     p = bf16_to_f32(p_bits)
@@ -77,7 +78,7 @@ def muon_apply(p_bits, upd_bits, lr: float, weight_decay: float, scale: float, s
     decay = f32(1.0 - lr * weight_decay)
     p = (p * decay).astype(f32)
     p = (p - f32(lr) * upd).astype(f32)
-    r = philox_randint(triton_key(seed), counters(p.size))
+    r = sr_noise(triton_key(seed), p.size, 0, noise)
     return sr_bf16(p, r)
 
 
@@ -91,7 +92,7 @@ def adamw_coefficients(lr, beta1, beta2, eps, weight_decay, step):
             f32(bc2s), f32(eps), f32(1.0 - lr * weight_decay))
 
 
-def adamw_sr(p_bits, g_bits, m_bits, v_bits, lr, beta1, beta2, eps, weight_decay, step, seed):
+def adamw_sr(p_bits, g_bits, m_bits, v_bits, lr, beta1, beta2, eps, weight_decay, step, seed, noise="reference"):
     """``_adamw_kernel`` -- ``muon_sr/triton_adamw.py:9-72``.
 
     Decay before the update; SR on ema (seed), ema_sq (seed + 1), p (seed + 2).
@@ -108,8 +109,7 @@ def adamw_sr(p_bits, g_bits, m_bits, v_bits, lr, beta1, beta2, eps, weight_decay
     denom = (np.sqrt(v) / bc2s + eps).astype(f32)
     p = (p * decay).astype(f32)
     p = (p - step_size * m / denom).astype(f32)
-    ctr = counters(p.size)
-    rm = philox_randint(triton_key(seed, 0), ctr)
-    rv = philox_randint(triton_key(seed, 1), ctr)
-    rp = philox_randint(triton_key(seed, 2), ctr)
+    rm = sr_noise(triton_key(seed, 0), p.size, 0, noise)
+    rv = sr_noise(triton_key(seed, 1), p.size, 0, noise)
+    rp = sr_noise(triton_key(seed, 2), p.size, 0, noise)
     return sr_bf16(p, rp), sr_bf16(m, rm), sr_bf16(v, rv)

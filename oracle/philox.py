@@ -63,3 +63,47 @@ def deterministic_seed(step: int, param_idx: int, salt: int = 0) -> int:
     """``_deterministic_seed`` -- ``muon_sr/triton_muon_sr.py:83-85``; AdamW uses salt 0
     (``triton_adamw.py:97``) and so does the 8-bit optimizer (``triton_adamw_8bit.py:197``)."""
     return (step * 2654435761 ^ param_idx * 1234567891 ^ salt) & 0xFFFFFFFF
+
+
+def philox4(key64: int, counters64) -> np.ndarray:
+    """All four Philox4x32-10 output words for 64-bit counters (ctr_lo32, ctr_hi32, 0, 0);
+    shape (n, 4), uint32."""
+    c = np.asarray(counters64).astype(np.uint64)
+    c0 = c & _M32
+    c1 = c >> np.uint64(32)
+    c2 = np.zeros_like(c0)
+    c3 = np.zeros_like(c0)
+    k0 = np.uint64(key64 & 0xFFFFFFFF)
+    k1 = np.uint64((key64 >> 32) & 0xFFFFFFFF)
+    for _ in range(10):
+        p0 = _MUL_A * c0
+        p2 = _MUL_B * c2
+        n0 = ((p2 >> np.uint64(32)) ^ c1 ^ k0) & _M32
+        n2 = ((p0 >> np.uint64(32)) ^ c3 ^ k1) & _M32
+        c1 = p2 & _M32
+        c3 = p0 & _M32
+        c0, c2 = n0, n2
+        k0 = (k0 + _KEY_A) & _M32
+        k1 = (k1 + _KEY_B) & _M32
+    return np.stack([c0, c1, c2, c3], axis=-1).astype(np.uint32)
+
+
+def fast_noise(key64: int, counters64) -> np.ndarray:
+    """The engine's opt-in fast noise stream (not the reference's): counter c takes the
+    16-bit half (c & 1) of output word ((c >> 1) & 3) of Philox4x32-10 at counter c >> 3."""
+    c = np.asarray(counters64).astype(np.uint64)
+    words = philox4(key64, c >> np.uint64(3))
+    k = (c & np.uint64(7)).astype(np.int64)
+    w = words[np.arange(c.size), k >> 1].astype(np.uint32)
+    return (w >> (16 * (k & 1)).astype(np.uint32)) & np.uint32(0xFFFF)
+
+
+def sr_noise(key64: int, n: int, ctr_base: int = 0, mode: str = "reference") -> np.ndarray:
+    """Noise words of ``n`` consecutive elements from ``ctr_base``: the reference's stream
+    (Philox word 0 at the offset truncated to 32 bits) or the fast one (64-bit counters)."""
+    ctr = np.arange(n, dtype=np.uint64) + np.uint64(ctr_base)
+    if mode == "reference":
+        return philox_randint(key64, ctr & _M32)
+    if mode == "fast":
+        return fast_noise(key64, ctr)
+    raise ValueError(f"unknown noise mode {mode!r}")

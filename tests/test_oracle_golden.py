@@ -102,3 +102,21 @@ def test_newton_schulz_cpu_matches_reference_bits():
         x = to_bf16(d[f"x{k}"]).view(*shp)
         y = newton_schulz(x, 5, None)
         assert_bits_equal(bits_of(y), d[f"y{k}"], f"NS shape {shp}")
+
+
+def test_fast_noise_stream_layout():
+    """The engine's fast stream is built from the same (golden-checked) Philox4x32-10: word
+    0 of the 4-word generator equals the reference's word for 32-bit counters, and counter c
+    takes 16-bit half c & 1 of word (c >> 1) & 3 at generator counter c >> 3."""
+    from oracle.philox import fast_noise, philox4, philox_randint
+    key = 0x0123456789ABCDEF
+    ctr = np.arange(0, 5000, 7, dtype=np.uint64)
+    assert np.array_equal(philox4(key, ctr)[:, 0], philox_randint(key, ctr))
+    c = np.arange(64, dtype=np.uint64) + np.uint64(3 * 2**32 + 5)
+    words = philox4(key, c >> np.uint64(3))
+    want = [(int(words[i, (int(x) >> 1) & 3]) >> (16 * (int(x) & 1))) & 0xFFFF for i, x in enumerate(c)]
+    assert fast_noise(key, c).tolist() == want
+    vals = fast_noise(key, np.arange(1 << 16, dtype=np.uint64))
+    assert vals.max() < 1 << 16
+    hist = np.bincount(vals >> 12, minlength=16)  # 16 bins of a uniform 16-bit value
+    assert hist.min() > 0.9 * (1 << 12) and hist.max() < 1.1 * (1 << 12)
