@@ -6,8 +6,8 @@ runs the step for the parameters it owns and the updated bf16 weights are then s
 NVLink / NVSwitch, so the step's work is divided by the number of ranks.
 
 * Partition: whole tensors (Newton-Schulz needs each full matrix), longest-processing-time
-  greedy on an estimated B200 time per tensor -- Newton-Schulz FLOPs at the tensor-core rate
-  for Muon matrices, bytes at the HBM rate for AdamW / 8-bit tensors.
+  greedy on an estimated B200 time per tensor -- Newton-Schulz FLOPs at its measured
+  effective rate for Muon matrices, bytes at the measured rate of each elementwise kernel.
 * Seeds and Philox counters stay global, so every rank writes exactly the bits a single GPU
   would (Newton-Schulz computes each matrix independently of how the batch is chunked).
 * Sharing: as soon as a segment of a shape stack (or a param group) is updated, its
@@ -27,8 +27,14 @@ import warnings
 import torch
 import torch.distributed as dist
 
-TENSOR_FLOPS = 1.4e15   # sustained dense bf16 on B200, used only to weigh the partition
-HBM_BYTES = 6.5e12
+# Rates that weigh the partition (measured on B200 inside the sharded step): Newton-Schulz at
+# its effective rate on the algorithmic FLOP count (symmetric tiles skip ~29%), and the
+# elementwise kernels at their achieved algorithmic bytes per second -- bound by the
+# reference's Philox noise stream, well below the HBM copy rate.
+TENSOR_FLOPS = 1.7e15
+MUON_EW_BYTES = 2.0e12     # prepare (8 B) + apply (6 B) per element
+ADAMW_BYTES = 1.0e12       # 14 B per element, three Philox streams
+ADAMW8BIT_BYTES = 1.28e12  # 10.0625 B per element
 SEGMENT_SECONDS = 4e-3  # per-rank Newton-Schulz time between two weight shares of a stack
 COPY_STREAMS_PER_PEER = 2
 
@@ -42,11 +48,21 @@ def _ns_flops(shape, steps=5):
     return batch * steps * (4 * m * m * n + 2 * m ** 3)
 
 
-def _cost(p, use_muon, ns_steps):
+def _kind(group):
+    """Kind of update a param group gets: Newton-Schulz (Muon), 8-bit AdamW or AdamW-SR."""
+    if group.get("use_muon", "momentum" in group and "betas" not in group):
+        return "muon"
+    return "adamw8bit" if "optim_bits" in group else "adamw"
+
+
+def _cost(p, kind, ns_steps):
+    """Estimated B200 seconds of one parameter's update."""
     numel = p.numel()
-    if use_muon and p.ndim >= 2:
-        return _ns_flops(tuple(p.shape), ns_steps) / TENSOR_FLOPS + 14 * numel / HBM_BYTES
-    return 14 * numel / HBM_BYTES
+    if kind == "muon" and p.ndim >= 2:
+        return _ns_flops(tuple(p.shape), ns_steps) / TENSOR_FLOPS + 14 * numel / MUON_EW_BYTES
+    if kind == "adamw8bit":
+        return 10.0625 * numel / ADAMW8BIT_BYTES
+    return 14 * numel / ADAMW_BYTES
 
 
 class Sharder:
@@ -99,9 +115,9 @@ class Sharder:
         """Assign every parameter to a rank (same result on every rank)."""
         entries = []
         for gi, g in enumerate(param_groups):
-            use_muon = g.get("use_muon", "momentum" in g and "betas" not in g)
+            kind = _kind(g)
             for pi, p in enumerate(g["params"]):
-                entries.append((_cost(p, use_muon, g.get("ns_steps", 5)), gi, pi, p))
+                entries.append((_cost(p, kind, g.get("ns_steps", 5)), gi, pi, p))
         # Largest first; ties broken by position so that the plan is deterministic.
         entries.sort(key=lambda e: (-e[0], e[1], e[2]))
         heap = [(0.0, r) for r in range(self.world)]
@@ -120,9 +136,9 @@ class Sharder:
         """Estimated seconds of work per rank under the current plan."""
         out = [0.0] * self.world
         for g in param_groups:
-            use_muon = g.get("use_muon", "momentum" in g and "betas" not in g)
+            kind = _kind(g)
             for p in g["params"]:
-                out[self._owner[id(p)]] += _cost(p, use_muon, g.get("ns_steps", 5))
+                out[self._owner[id(p)]] += _cost(p, kind, g.get("ns_steps", 5))
         return out
 
     def _ensure(self, optimizer):
