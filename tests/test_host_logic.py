@@ -237,3 +237,65 @@ def test_sharder_segment_counts():
             got = sh.segments(shape, n)
             assert got == want, (world, shape, got)
             assert got == 1 or n // got >= 2 * world
+
+
+def _record_batched_step(rank, world, random_seeds, drop_grad=None, segments=None):
+    """Run muon.muon_batch_step on CPU tensors with recording fakes in place of the CUDA
+    kernels; returns (per-matrix apply seeds, prepare calls, share calls)."""
+    import muon_sr_b200.muon as M
+    shapes = [(8, 16)] * 6 + [(16, 8)] * 3 + [(4, 4)] * 2
+    params = [torch.nn.Parameter(torch.zeros(*s, dtype=torch.bfloat16)) for s in shapes]
+    for i, p in enumerate(params):
+        p.grad = None if i == drop_grad else torch.zeros_like(p)
+    state = {p: {} for p in params}
+    stacks = M._MomentumStacks(params, state)
+    log = {"apply": {}, "prepare": [], "share": []}
+    names = {id(p): i for i, p in enumerate(params)}
+
+    def prepare(items, beta, nesterov):
+        log["prepare"].append([(int(ctr), int(seed)) for _, _, _, ctr, seed in items])
+
+    def ns(x, steps):
+        return torch.zeros_like(x)
+
+    def apply(items, lr, wd):
+        for p, _, _, seed in items:
+            log["apply"][names[id(p)]] = int(seed)
+
+    saved = (M.K.muon_prepare, M.K.newton_schulz, M.K.muon_apply)
+    M.K.muon_prepare, M.K.newton_schulz, M.K.muon_apply = prepare, ns, apply
+    try:
+        owner = (lambda s, r: (s * 7 + r) % world == rank) if world > 1 else None
+        share = (lambda ps: log["share"].append([names[id(p)] for p in ps])) if world > 1 else None
+        torch.manual_seed(99)
+        M.muon_batch_step(stacks, 0.95, True, 5, 0.02, 0.0, 7, M._Seeder(random_seeds),
+                          M._Work(owner, share, segments))
+    finally:
+        M.K.muon_prepare, M.K.newton_schulz, M.K.muon_apply = saved
+    return log
+
+
+@pytest.mark.parametrize("random_seeds", [False, True])
+@pytest.mark.parametrize("drop_grad", [None, 7])
+def test_batched_step_sharding_logic(random_seeds, drop_grad):
+    """Two simulated ranks together update every matrix exactly once, with the seed the
+    single-process step uses (deterministic or drawn from torch's generator, also in the
+    partial-gradient fallback), and call the share hook with the same sequence; segmented
+    sharing changes neither."""
+    single = _record_batched_step(0, 1, random_seeds, drop_grad)
+    seg = (lambda shape, n: 2)
+    for segments in (None, seg):
+        logs = [_record_batched_step(r, 2, random_seeds, drop_grad, segments) for r in range(2)]
+        merged = {}
+        for lg in logs:
+            assert not set(merged) & set(lg["apply"]), "a matrix was updated by both ranks"
+            merged.update(lg["apply"])
+        assert merged == single["apply"]
+        assert logs[0]["share"] == logs[1]["share"]
+        if segments is not None and drop_grad is None:
+            assert len(logs[0]["share"]) > len(_record_batched_step(0, 2, random_seeds, drop_grad)["share"])
+    if drop_grad is None:
+        # prepare counters run over each whole stack (row r starts at r * numel) on every rank
+        ctrs = sorted(c for lg in (_record_batched_step(r, 2, random_seeds) for r in range(2))
+                      for call in lg["prepare"] for c, _ in call)
+        assert ctrs == sorted(c for call in single["prepare"] for c, _ in call)
