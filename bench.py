@@ -375,7 +375,7 @@ def run_ours(args, rank, world, local_rank):
             "elementwise_hbm_gbs": ew_rates(breakdown),
             "fast_noise": fast_noise,
             "breakdown_ms_per_step_per_rank": per_rank if world > 1 else None,
-            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (Newton-Schulz chain)",
+            "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (Newton-Schulz chain)",
                          "achieved": ns_tflops, "peak": peak_ns, "unit": "TFLOP/s",
                          "frac": (ns_tflops / peak_ns) if ns_tflops else None,
                          "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None,
@@ -399,40 +399,51 @@ def run_ours(args, rank, world, local_rank):
 # ---------------------------------------------------------------------------------------
 # CPU (reference) arm -- the reference's pure-PyTorch MuonSR / AdamW-SR restated in oracle/
 # ---------------------------------------------------------------------------------------
+CPU_SAMPLE = ("per step: one MuonSR parameter step (oracle.muon_cpu, restating muon_sr/muon_sr.py) for each of "
+              "the four distinct Llama-3-8B matrix shapes, each scaled by that shape's count, plus an AdamW-SR "
+              "step on a 2^23-element slice scaled by elements to the 1.05G-element AdamW group")
+
+
 def cpu_sample_step(threads):
-    """One bounded sample of the full Llama step on the host cores: one q_proj-shaped
-    (4096 x 4096) MuonSR parameter step and an AdamW-SR step on a 2^22-element slice.
-    Returns (seconds of the sample, extrapolation factor to a full step)."""
+    """One bounded sample of the full Llama step on the host cores: a MuonSR parameter step
+    for one matrix of each distinct shape (q/o, k/v, gate/up, down), each scaled by that
+    shape's count, and an AdamW-SR step on a 2^23-element slice scaled by elements.
+    Returns (extrapolated milliseconds per full step, seconds of CPU work in the sample)."""
     from oracle.muon_cpu import adamw_sr_step, muon_sr_step
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
-    shape = (D, D)
-    p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
-    gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
-    b = torch.zeros_like(p)
-    n_slice = 1 << 22
+    muon_shapes, adam_shapes = llama_shapes()
+    counts = {}
+    for s in muon_shapes:
+        counts[s] = counts.get(s, 0) + 1
+    full = 0.0
+    work = 0.0
+    for shape, count in counts.items():
+        p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+        gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
+        b = torch.zeros_like(p)
+        t0 = time.perf_counter()
+        muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
+        dt = time.perf_counter() - t0
+        full += dt * count
+        work += dt
+    n_slice = 1 << 23
     pa = (torch.randn(n_slice, generator=g) * 0.02).bfloat16()
     ga = (torch.randn(n_slice, generator=g) * 1e-3).bfloat16()
     ea, eb = torch.zeros_like(pa), torch.zeros_like(pa)
     t0 = time.perf_counter()
-    muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
-    t1 = time.perf_counter()
     adamw_sr_step([pa], [ga], [ea], [eb], 1, weight_decay=0.01)
-    t2 = time.perf_counter()
-    muon_shapes, adam_shapes = llama_shapes()
-    f_total = sum(ns_flops(s) for s in muon_shapes)
-    n_adam = sum(math.prod(s) for s in adam_shapes)
-    full = (t1 - t0) * f_total / ns_flops(shape) + (t2 - t1) * n_adam / n_slice
-    return full * 1e3, t2 - t0
+    dt = time.perf_counter() - t0
+    full += dt * sum(math.prod(s) for s in adam_shapes) / n_slice
+    work += dt
+    return full * 1e3, work
 
 
 def run_reference(args, rank):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    sample = ("per step: one 4096x4096 MuonSR parameter step (oracle.muon_cpu, restating muon_sr/muon_sr.py) "
-              "scaled by Newton-Schulz FLOPs to all 224 matrices, plus a 4.2M-element AdamW-SR slice scaled "
-              "by elements to the 1.05G-element AdamW group")
+    sample = CPU_SAMPLE
     for _ in range(args.warmup):
         cpu_sample_step(threads)
     vals = [cpu_sample_step(threads)[0] for _ in range(args.steps)]
@@ -539,8 +550,7 @@ def main():
             if world == 1 and not args.no_cpu_baseline:
                 v, secs = cpu_sample_step(os.cpu_count() or 1)
                 out["cpu_baseline"] = {"value": v, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
-                                       "sample": f"one 4096x4096 MuonSR step + 4.2M-element AdamW-SR slice "
-                                                 f"({secs:.1f} s of CPU work), scaled to the full step"}
+                                       "sample": f"{CPU_SAMPLE} ({secs:.1f} s of CPU work)"}
             print(json.dumps(out), flush=True)
     finally:
         if world > 1:
