@@ -301,6 +301,16 @@ def run_ours(args, rank, world, local_rank):
         a8_bytes_rank = a8_bytes
         a8_elems_rank = n_all
     a8_gbs = a8_bytes_rank / (a8_kernel_ms * 1e-3) / 1e9 if a8_kernel_ms > 0 else None
+    # the same 8-bit step with the opt-in fast noise stream
+    K.set_sr_noise("fast")
+    a8_timers.events.clear()
+    a8_timers.enabled = True
+    a8_fast_step_ms = time_steps(opt8.step, args.steps, 1, world)
+    a8_fast_kernel_ms = a8_timers.totals_ms().get("adamw8bit", 0.0) / (args.steps + 1)
+    a8_timers.enabled = False
+    K.set_sr_noise("reference")
+    fast_noise["adamw8bit_step_ms"] = a8_fast_step_ms
+    fast_noise["adamw8bit_hbm_gbs"] = a8_bytes_rank / (a8_fast_kernel_ms * 1e-3) / 1e9 if a8_fast_kernel_ms else None
     del opt8
     torch.cuda.empty_cache()
 
