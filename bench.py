@@ -409,14 +409,14 @@ def run_ours(args, rank, world, local_rank):
 # ---------------------------------------------------------------------------------------
 # CPU (reference) arm -- the reference's pure-PyTorch MuonSR / AdamW-SR restated in oracle/
 # ---------------------------------------------------------------------------------------
-CPU_SAMPLE = ("per step: one MuonSR parameter step (oracle.muon_cpu, restating muon_sr/muon_sr.py) for each of "
-              "the four distinct Llama-3-8B matrix shapes, each scaled by that shape's count, plus an AdamW-SR "
+CPU_SAMPLE = ("per step: three MuonSR parameter steps (oracle.muon_cpu, restating muon_sr/muon_sr.py) for each "
+              "of the four distinct Llama-3-8B matrix shapes, scaled by that shape's count, plus an AdamW-SR "
               "step on a 2^23-element slice scaled by elements to the 1.05G-element AdamW group")
 
 
 def cpu_sample_step(threads):
-    """One bounded sample of the full Llama step on the host cores: a MuonSR parameter step
-    for one matrix of each distinct shape (q/o, k/v, gate/up, down), each scaled by that
+    """One bounded sample of the full Llama step on the host cores: MuonSR parameter steps
+    for three matrices of each distinct shape (q/o, k/v, gate/up, down), scaled by that
     shape's count, and an AdamW-SR step on a 2^23-element slice scaled by elements.
     Returns (extrapolated milliseconds per full step, seconds of CPU work in the sample)."""
     from oracle.muon_cpu import adamw_sr_step, muon_sr_step
@@ -428,15 +428,17 @@ def cpu_sample_step(threads):
         counts[s] = counts.get(s, 0) + 1
     full = 0.0
     work = 0.0
+    per_shape = 3  # matrices sampled per distinct shape
     for shape, count in counts.items():
-        p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
-        gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
-        b = torch.zeros_like(p)
-        t0 = time.perf_counter()
-        muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
-        dt = time.perf_counter() - t0
-        full += dt * count
-        work += dt
+        for _ in range(per_shape):
+            p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+            gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
+            b = torch.zeros_like(p)
+            t0 = time.perf_counter()
+            muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
+            dt = time.perf_counter() - t0
+            full += dt * count / per_shape
+            work += dt
     n_slice = 1 << 23
     pa = (torch.randn(n_slice, generator=g) * 0.02).bfloat16()
     ga = (torch.randn(n_slice, generator=g) * 1e-3).bfloat16()
