@@ -51,3 +51,28 @@ def test_ns_workspace_accounts_for_padding():
     plain = lib.msr_ns_workspace_bytes(4, 64, 128)
     padded = lib.msr_ns_workspace_bytes(4, 63, 127)
     assert plain > 0 and padded > plain  # padded shapes need two more staging buffers
+
+
+def test_more_argument_errors_without_gpu():
+    """Every entry point rejects bad arguments with MSR_ERR_INVALID (1) and a message before
+    it touches a device."""
+    lib = _lib.load()
+    assert lib.msr_set_sr_noise(7) == 1 and b"unknown mode" in lib.msr_last_error()
+    assert lib.msr_set_sr_noise(0) == 0
+    assert lib.msr_test_wait_timeout(0, None) == 1
+    assert lib.msr_centralize_bf16(None, None, 4, 4, 0.5, None) == 1
+    assert lib.msr_gemm_bf16(None, 0, None, 0, None, None, 1, 8, 8, 8, 1.0, 0.0, None, 0, 0, 0, None) == 1
+    assert lib.msr_newton_schulz_bf16(None, None, 1, 8, 8, 5, 9, None, None, 0, None) == 1
+    assert lib.msr_newton_schulz_bf16_noalloc(None, None, 1, 8, 8, 5, 0, None, None) == 1
+    assert lib.msr_muon_prepare(None, -1, 0.9, 0.1, 1, None) == 1
+    assert lib.msr_muon_apply(None, -1, 0.02, 1.0, None) == 1
+    assert lib.msr_adamw_sr(None, -1, None, None) == 1
+    assert lib.msr_adamw8bit(None, -1, None, None, None, None) == 1
+    assert lib.msr_copy_async(None, None, 16, None) == 1
+    assert lib.msr_ipc_export(None, None, None) == 1
+    assert lib.msr_ipc_import(None, None) == 1
+    assert lib.msr_ipc_event_create(None, None) == 1
+    assert lib.msr_ipc_event_open(None, None) == 1
+    # zero-length and empty requests are no-ops
+    assert lib.msr_copy_async(None, None, 0, None) == 0
+    assert lib.msr_muon_prepare(None, 0, 0.9, 0.1, 1, None) == 0
