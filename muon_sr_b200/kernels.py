@@ -159,9 +159,11 @@ _workspaces = {}
 
 
 def _workspace(device, nbytes: int) -> torch.Tensor:
-    """Per-device scratch buffer for the Newton-Schulz chain, grown on demand (stream-ordered
-    reuse on the current stream)."""
-    key = torch.device(device).index
+    """Scratch buffer for the Newton-Schulz chain, one per (device, stream) and grown on
+    demand: calls on one stream reuse it in stream order, calls on different streams never
+    share it."""
+    device = torch.device(device)
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         _workspaces[key] = ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
