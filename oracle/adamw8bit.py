@@ -7,7 +7,6 @@ walk); bitsandbytes itself is not installed here and is not needed: parity is an
 the reference's own code run under the Triton interpreter.
 """
 import numpy as np
-import torch
 
 from .philox import sr_noise, triton_key
 from .sr import bf16_to_f32, sr_bf16
@@ -15,17 +14,38 @@ from .sr import bf16_to_f32, sr_bf16
 f32 = np.float32
 
 
+def _fma32(a, b, c):
+    """fp32 fused multiply-add: the product of two fp32 values is exact in float64, and for
+    the magnitudes used here (grid points in [0.1, 1]) so is the sum, so one rounding to fp32
+    gives the fused result."""
+    return f32(np.float64(a) * np.float64(b) + np.float64(c))
+
+
+def _linspace_f32(start, end, steps):
+    """torch's fp32 ``linspace`` on the CPU: step = (end - start) / (steps - 1) in fp32; the
+    first half of the points is start + step * i, the second end - step * (steps - 1 - i),
+    each as one fused multiply-add (checked bit-exact against torch for 2..129 points)."""
+    s, e = f32(start), f32(end)
+    step = f32((e - s) / f32(steps - 1))
+    half = steps // 2
+    return np.array([_fma32(step, f32(i), s) if i < half else _fma32(-step, f32(steps - 1 - i), e)
+                     for i in range(steps)], dtype=f32)
+
+
 def create_dynamic_map(signed: bool = True) -> np.ndarray:
-    """``create_dynamic_map`` -- ``triton_adamw_8bit.py:14-25``. Built with torch fp32
-    ``linspace`` and fp32 scaling exactly as the reference does, so the table bits agree."""
-    data = []
-    for i in range(7):
-        boundaries = torch.linspace(0.1, 1, 2 ** (i if signed else i + 1) + 1, dtype=torch.float32)
-        means = (boundaries[:-1] + boundaries[1:]) / 2
-        data.extend((10 ** (-6 + i) * means).tolist())
+    """``create_dynamic_map`` -- ``triton_adamw_8bit.py:14-25``, restated in numpy: for decade
+    k = 0..6 the fp32 midpoints of a ``linspace(0.1, 1)`` grid of 2^k intervals (2^(k+1) for
+    the unsigned map) scaled by fp32(10^(k-6)), mirrored for the signed map, plus 0 and 1,
+    sorted. Pinned against the reference's table by the golden codebooks."""
+    vals = [f32(0.0), f32(1.0)]
+    for k in range(7):
+        grid = _linspace_f32(0.1, 1.0, (1 << (k if signed else k + 1)) + 1)
+        mids = ((grid[:-1] + grid[1:]) / f32(2)).astype(f32)
+        scaled = (f32(10.0 ** (k - 6)) * mids).astype(f32)
+        vals.extend(scaled)
         if signed:
-            data.extend((-10 ** (-6 + i) * means).tolist())
-    return np.array(sorted(data + [0.0, 1.0]), dtype=np.float32)
+            vals.extend(-scaled)
+    return np.sort(np.array(vals, dtype=f32))
 
 
 def quantize(x, Q, signed: bool) -> np.ndarray:
