@@ -12,6 +12,7 @@ from .adamw8bit import TritonAdamW8bit, create_dynamic_map
 from .muon import MuonSR, MuonSRWithAuxAdam, TritonMuonSR, TritonMuonSRWithAuxAdam
 from .kernels import set_sr_noise
 from .sharding import Sharder
+from .staging import HostStaging
 
 __all__ = [
     "SRAccumulator",
@@ -19,5 +20,5 @@ __all__ = [
     "TritonAdamW", "TritonSRAccumulator",
     "MuonSR", "MuonSRWithAuxAdam",
     "TritonMuonSR", "TritonMuonSRWithAuxAdam",
-    "Sharder", "create_dynamic_map", "set_sr_noise",
+    "Sharder", "HostStaging", "create_dynamic_map", "set_sr_noise",
 ]

@@ -9,6 +9,7 @@ import torch
 from torch.optim import Optimizer
 
 from . import kernels as K
+from . import staging
 from .seeds import deterministic_seed
 
 
@@ -21,9 +22,10 @@ def adamw_group_step(state, group, offset, seed_of, owns=None, centralization=0.
     parameters in earlier groups; then the whole group in one multi-tensor launch. ``owns(i)``
     restricts the kernel work to this rank's parameters (state and seeds still advance, so
     every rank stays in step). ``centralization`` != 0 first centres each gradient with the
-    fused kernel (triton_adamw.py:179-187)."""
+    fused kernel (triton_adamw.py:179-187). While a ``staging.HostStaging`` step runs, the
+    launch is cut into batches of whole parameters so that uploads overlap updates."""
     beta1, beta2 = group["betas"]
-    batch = []
+    todo = []
     for i, p in enumerate(group["params"]):
         assert p.dtype == torch.bfloat16, "only bfloat16 is supported."
         if p.grad is None:
@@ -40,9 +42,15 @@ def adamw_group_step(state, group, offset, seed_of, owns=None, centralization=0.
             continue
         if p.grad.dtype != torch.bfloat16:
             raise ValueError("gradients must be bfloat16")
-        grad = K.centralize(p.grad, centralization) if centralization else p.grad.contiguous()
-        batch.append((p, grad, st["ema"], st["ema_squared"], st["step"], seed))
-    K.adamw_sr(batch, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
+        todo.append((p, st, seed))
+    for part in staging.batches(todo, lambda e: e[0].numel()):
+        staging.need([p for p, _, _ in part])
+        batch = []
+        for p, st, seed in part:
+            grad = K.centralize(p.grad, centralization) if centralization else p.grad.contiguous()
+            batch.append((p, grad, st["ema"], st["ema_squared"], st["step"], seed))
+        K.adamw_sr(batch, group["lr"], beta1, beta2, group["eps"], group["weight_decay"])
+        staging.done([p for p, _, _ in part])
 
 
 class TritonAdamW(Optimizer):

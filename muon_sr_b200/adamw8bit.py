@@ -12,6 +12,7 @@ import torch
 from torch.optim import Optimizer
 
 from . import kernels as K
+from . import staging
 
 
 def create_dynamic_map(signed=True):
@@ -180,8 +181,11 @@ class TritonAdamW8bit(Optimizer):
                     if tkey not in self._qtables:  # built once per codebook pair (host copy of 2 KB)
                         self._qtables[tkey] = K.quant_tables(maps[0], maps[1])
                     tables = self._qtables[tkey]
-                K.adamw8bit(items, maps[0], maps[1], group['lr'], b1, b2, group['eps'], group['weight_decay'],
-                            group['block_size'], qtables=tables)
+                for part in staging.batches(items, lambda e: e[0].numel()):
+                    staging.need([e[0] for e in part])
+                    K.adamw8bit(part, maps[0], maps[1], group['lr'], b1, b2, group['eps'], group['weight_decay'],
+                                group['block_size'], qtables=tables)
+                    staging.done([e[0] for e in part])
         if self._shard:
             self._shard.sync_params(self)
         return loss

@@ -18,6 +18,7 @@ import torch
 from torch.optim import Optimizer
 
 from . import kernels as K
+from . import staging
 from .adamw import adamw_group_step
 from .seeds import deterministic_seed
 
@@ -106,14 +107,16 @@ def _validate(p, name):
 # ---------------------------------------------------------------------------------------
 # Muon updates
 # ---------------------------------------------------------------------------------------
-def muon_single_step(p, grad, buf, beta, nesterov, ns_steps, lr, weight_decay, step, param_idx, seeder):
+def muon_single_step(p, buf, beta, nesterov, ns_steps, lr, weight_decay, step, param_idx, seeder):
     """Per-parameter Muon step (``_triton_muon_step``, triton_muon_sr.py:116-120)."""
     if p.ndim < 2:
         raise AssertionError("Newton-Schulz needs ndim >= 2 parameters")
+    staging.need([p])
     update = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
-    K.muon_prepare([(grad, buf, update, 0, seeder(step, param_idx, 0))], beta, nesterov)
+    K.muon_prepare([(_grad_of(p), buf, update, 0, seeder(step, param_idx, 0))], beta, nesterov)
     out = K.newton_schulz(update, ns_steps)
     K.muon_apply([(p, out, K.ns_scale(p.shape), seeder(step, param_idx, 1))], lr, weight_decay)
+    staging.done([p])
 
 
 def _segments(n, count):
@@ -139,9 +142,12 @@ def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, se
     """Batched step over the shape stacks (``_triton_muon_batch_step``,
     triton_muon_sr.py:128-177).
 
-    For stack number s of ``stacks.by_shape`` (first-appearance order): prepare over the whole
-    stack with seed S(step, s, 0) and counters running over the stack; Newton-Schulz on chunks
-    of at most NS_CHUNK_NUMEL elements; apply of row r with S(step, s * 10000 + r, 1). A stack
+    For stack number s of ``stacks.by_shape`` (first-appearance order): prepare with seed
+    S(step, s, 0) and counters running over the whole stack; Newton-Schulz on chunks of at most
+    NS_CHUNK_NUMEL elements; apply of row r with S(step, s * 10000 + r, 1). Prepare, Newton-
+    Schulz and apply are issued chunk by chunk (the prepare's counters are those of the whole
+    stack, so the bits are the reference's), which keeps the scratch at one chunk and lets a
+    ``staging.HostStaging`` step upload the next chunk's gradients meanwhile. A stack
     where only some parameters have gradients falls back to per-parameter steps with
     param_idx = s * 10000 + r. With ``work`` only this rank's rows are computed (seeds and
     counters stay global, so results do not depend on the number of ranks) and the weights
@@ -173,8 +179,8 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
             if p.grad is None:
                 continue
             if work.mine(s, r):
-                muon_single_step(p, _grad_of(p), momentum[r], beta, nesterov, ns_steps, lr, weight_decay, step,
-                                 s * 10000 + r, seeder)
+                muon_single_step(p, momentum[r], beta, nesterov, ns_steps, lr, weight_decay, step, s * 10000 + r,
+                                 seeder)
             else:
                 seeder.skip(step, s * 10000 + r, 0)
                 seeder.skip(step, s * 10000 + r, 1)
@@ -188,22 +194,26 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
     # row in row order (all of them on every rank)
     prep_seed = seeder(step, s, 0)
     apply_seed = [seeder(step, s * 10000 + r, 1) for r in range(len(members))]
-    upd = None
-    if rows:
-        upd = torch.empty((len(rows),) + tuple(shape), dtype=torch.bfloat16, device=momentum.device)
-        K.muon_prepare([(_grad_of(members[r]), momentum[r], upd[j], r * numel, prep_seed) for j, r in enumerate(rows)],
-                       beta, nesterov)
     chunk = max(1, NS_CHUNK_NUMEL // max(1, numel))
     scale = K.ns_scale(shape)
-    lo = 0  # first position in `rows` (and `upd`) of the current segment
+    upd = torch.empty((min(chunk, len(rows)),) + tuple(shape), dtype=torch.bfloat16, device=momentum.device) \
+        if rows else None
+    lo = 0  # first position in `rows` of the current segment
     for part in parts:
         hi = lo
         while hi < len(rows) and rows[hi] in part:
             hi += 1
         for c in range(lo, hi, chunk):
-            out = K.newton_schulz(upd[c:min(c + chunk, hi)], ns_steps)
-            K.muon_apply([(members[rows[c + j]], out[j], scale, apply_seed[rows[c + j]]) for j in range(out.shape[0])],
-                         lr, weight_decay)
+            # prepare of the chunk's rows with the stack's seed and counters: the same bits as
+            # one prepare over the whole stack
+            mine = [members[rows[c + j]] for j in range(min(chunk, hi - c))]
+            staging.need(mine)
+            x = upd[:len(mine)]
+            K.muon_prepare([(_grad_of(p), momentum[rows[c + j]], x[j], rows[c + j] * numel, prep_seed)
+                            for j, p in enumerate(mine)], beta, nesterov)
+            out = K.newton_schulz(x, ns_steps)
+            K.muon_apply([(p, out[j], scale, apply_seed[rows[c + j]]) for j, p in enumerate(mine)], lr, weight_decay)
+            staging.done(mine)
             del out
         lo = hi
         if len(parts) > 1:
@@ -266,7 +276,7 @@ class _MuonBase(Optimizer):
                 seeder.skip(step, i, 0)
                 seeder.skip(step, i, 1)
                 continue
-            muon_single_step(p, _grad_of(p), st["momentum_buffer"], beta, nesterov, ns_steps, lr, wd, step, i, seeder)
+            muon_single_step(p, st["momentum_buffer"], beta, nesterov, ns_steps, lr, wd, step, i, seeder)
         if sh:
             sh.share(group["params"])
 

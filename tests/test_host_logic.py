@@ -299,3 +299,61 @@ def test_batched_step_sharding_logic(random_seeds, drop_grad):
         ctrs = sorted(c for lg in (_record_batched_step(r, 2, random_seeds) for r in range(2))
                       for call in lg["prepare"] for c, _ in call)
         assert ctrs == sorted(c for call in single["prepare"] for c, _ in call)
+
+
+class _RecordingIO:
+    """Stands in for a HostStaging: records the announcements of a step."""
+
+    def __init__(self, log, names):
+        self.log, self.names = log, names
+
+    def need(self, params):
+        self.log.append(("need", [self.names[id(p)] for p in params]))
+
+    def done(self, params):
+        self.log.append(("done", [self.names[id(p)] for p in params]))
+
+
+def test_batched_step_staging_hooks(monkeypatch):
+    """A batched Muon step announces each Newton-Schulz chunk: its gradients are needed before
+    the chunk's prepare, and its weights are done after the chunk's apply; every matrix with a
+    gradient is announced exactly once, and the prepare counters are those of the whole stack."""
+    import muon_sr_b200.muon as M
+    import muon_sr_b200.staging as S
+    shapes = [(8, 16)] * 5 + [(16, 8)] * 3
+    params = [torch.nn.Parameter(torch.zeros(*s, dtype=torch.bfloat16)) for s in shapes]
+    for p in params:
+        p.grad = torch.zeros_like(p)
+    names = {id(p): i for i, p in enumerate(params)}
+    stacks = M._MomentumStacks(params, {p: {} for p in params})
+    log = []
+    monkeypatch.setattr(M, "NS_CHUNK_NUMEL", 256)   # 2 matrices per chunk
+    monkeypatch.setattr(M.K, "muon_prepare", lambda items, b, n: log.append(
+        ("prepare", [int(ctr) for _, _, _, ctr, _ in items])))
+    monkeypatch.setattr(M.K, "newton_schulz", lambda x, steps: torch.zeros_like(x))
+    monkeypatch.setattr(M.K, "muon_apply", lambda items, lr, wd: log.append(
+        ("apply", [names[id(p)] for p, _, _, _ in items])))
+    monkeypatch.setattr(S._tls, "io", _RecordingIO(log, names), raising=False)
+    M.muon_batch_step(stacks, 0.95, True, 5, 0.02, 0.0, 3, M._Seeder(False))
+    kinds = [k for k, _ in log]
+    assert kinds == ["need", "prepare", "apply", "done"] * 5   # chunks: 2+2+1 and 2+1 matrices
+    needs = [v for k, v in log if k == "need"]
+    assert needs == [v for k, v in log if k == "apply"] == [v for k, v in log if k == "done"]
+    assert sorted(i for v in needs for i in v) == list(range(8))
+    ctrs = [c for k, v in log if k == "prepare" for c in v]
+    assert ctrs == [r * 128 for r in range(5)] + [r * 128 for r in range(3)]
+
+
+def test_staging_batches():
+    """Launch batches are cut only while a staging step runs, at whole items."""
+    import muon_sr_b200.staging as S
+    items = [1 << 27, 1 << 27, 1 << 27, 1 << 29, 5]
+    assert S.batches(items, lambda n: n) == [items]
+    assert S.batches([], lambda n: n) == []
+    S._tls.io = object()
+    try:
+        got = S.batches(items, lambda n: n)
+    finally:
+        S._tls.io = None
+    assert got == [[1 << 27, 1 << 27], [1 << 27], [1 << 29], [5]]
+    assert [x for b in got for x in b] == items
