@@ -46,8 +46,11 @@ int msr_abi_version(void);
  *     c uses 16-bit half (c & 1) of output word ((c >> 1) & 3) at counter (c >> 3), same
  *     keys. Each value is still rounded up with probability equal to its fractional part
  *     (unbiased stochastic rounding), but the bits differ from the reference's.
+ *   MSR_SR_NOISE_NONE -- no stochastic rounding: every SR store rounds to the nearest bf16
+ *     (ties to even) instead, as a plain fp32 -> bf16 cast would. A parity mode for checking
+ *     the fp32 arithmetic of the updates without noise; not for training.
  * Returns MSR_ERR_INVALID for an unknown mode. */
-enum msr_sr_noise { MSR_SR_NOISE_REFERENCE = 0, MSR_SR_NOISE_FAST = 1 };
+enum msr_sr_noise { MSR_SR_NOISE_REFERENCE = 0, MSR_SR_NOISE_FAST = 1, MSR_SR_NOISE_NONE = 2 };
 int msr_set_sr_noise(int mode);
 /* Static description of a status code. */
 const char* msr_status_string(int status);

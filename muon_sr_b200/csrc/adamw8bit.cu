@@ -123,8 +123,9 @@ __device__ __forceinline__ float group_max(float v, float* red) {
 constexpr size_t smem_for(bool tables) { return 2 * 256 * 4 + (tables ? MSR_QT_BYTES : 0); }
 
 // EPT elements per thread, BS elements per quantisation block.
-template <int BS, bool TABLES, bool FAST>
+template <int BS, bool TABLES, int NOISE>
 __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_constant__ Adam8Args a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
   constexpr int EPT = BS > 2048 ? 16 : 8;
   constexpr int TILE = Q_THREADS * EPT;
   constexpr int G = BS / EPT;  // threads per quantisation block
@@ -158,7 +159,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
     uint16_t* P = static_cast<uint16_t*>(E.param);
     const uint16_t* Gp = static_cast<const uint16_t*>(E.grad);
     const bool vec = a.vec[ei] && base + EPT <= n;
-    const SrNoise<FAST> np_{make_key(E.key_p)};
+    const SrNoise<NOISE> np_{make_key(E.key_p)};
 
     uint16_t pb[EPT], gb[EPT];
     if (vec) {
@@ -247,7 +248,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
       const float p = bf16_bits_to_f32(pb[j]);
       const float upd = fsub(p, __fdiv_rn(fmul(E.coef, m[j]), fadd(__fsqrt_rn(v[j]), E.sqrt_bc2_eps)));
       const float updated = fmul(upd, hp.decay);
-      if (fin) pb[j] = sr_bf16_bits(updated, FAST ? rp[j] : np_.at(static_cast<uint64_t>(base + j)));
+      if (fin) pb[j] = round_bf16<NOISE>(updated, FAST ? rp[j] : np_.at(static_cast<uint64_t>(base + j)));
       if (base + j < n) {
         mmax = fmaxf(mmax, fabsf(m[j]));
         vmax = fmaxf(vmax, fabsf(v[j]));
@@ -313,7 +314,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
         E.absmax2[base / BS] = vmax;
       }
     } else {
-      const SrNoise<FAST> nm{make_key(E.key_m)}, nv{make_key(E.key_v)};
+      const SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)};
       uint16_t* S1 = static_cast<uint16_t*>(E.state1);
       uint16_t* S2 = static_cast<uint16_t*>(E.state2);
       uint16_t mb[EPT], vb[EPT];
@@ -328,8 +329,8 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
 #pragma unroll
       for (int j = 0; j < EPT; ++j) {
         const uint64_t ctr = static_cast<uint64_t>(base + j);
-        mb[j] = sr_bf16_bits(m[j], FAST ? rm[j] : nm.at(ctr));
-        vb[j] = sr_bf16_bits(v[j], FAST ? rv[j] : nv.at(ctr));
+        mb[j] = round_bf16<NOISE>(m[j], FAST ? rm[j] : nm.at(ctr));
+        vb[j] = round_bf16<NOISE>(v[j], FAST ? rv[j] : nv.at(ctr));
       }
       if (vec) {
 #pragma unroll
@@ -349,25 +350,28 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
   }
 }
 
-template <int BS, bool TABLES, bool FAST>
+template <int BS, bool TABLES, int NOISE>
 int launch_variant(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
   const int64_t cap = static_cast<int64_t>(sm_count()) * Q_BLOCKS_PER_SM;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
   constexpr size_t smem = smem_for(TABLES);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES, NOISE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
-  adamw8bit_kernel<BS, TABLES, FAST><<<grid, Q_THREADS, smem, s>>>(a);
+  adamw8bit_kernel<BS, TABLES, NOISE><<<grid, Q_THREADS, smem, s>>>(a);
   return check_launch("adamw8bit_kernel");
+}
+
+template <int BS, int NOISE>
+int launch_noise(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
+  return a.hp.qtables ? launch_variant<BS, true, NOISE>(a, tiles, s) : launch_variant<BS, false, NOISE>(a, tiles, s);
 }
 
 template <int BS>
 int launch_bs(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
-  if (sr_noise_fast())
-    return a.hp.qtables ? launch_variant<BS, true, true>(a, tiles, s) : launch_variant<BS, false, true>(a, tiles, s);
-  return a.hp.qtables ? launch_variant<BS, true, false>(a, tiles, s) : launch_variant<BS, false, false>(a, tiles, s);
+  return pick_noise(launch_noise<BS, NOISE_REF>, launch_noise<BS, NOISE_FAST>, launch_noise<BS, NOISE_NONE>)(a, tiles, s);
 }
 
 inline bool al(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

@@ -81,31 +81,41 @@ __device__ __forceinline__ uint4 philox4(uint64_t ctr, PhiloxKey key) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Stochastic-rounding noise streams (the low 16 bits of each value are used)
-//  * SrNoise<false> -- the reference's: word 0 of Philox4x32-10 at the counter truncated to
-//    32 bits, one generator call per rounded value (bit-identical to muon_sr).
-//  * SrNoise<true>  -- fast mode (msr_set_sr_noise): one generator call per 8 consecutive
-//    counters; counter c uses the 16-bit half (c & 1) of word ((c >> 1) & 3) of Philox4x32-10
-//    at counter (c >> 3) (64-bit). Same keys. Statistically an unbiased 16-bit uniform per
-//    value like the reference's, but different bits.
+// Stochastic-rounding noise streams (the low 16 bits of each value are used), one per
+// msr_sr_noise mode:
+//  * SrNoise<NOISE_REF>  -- the reference's: word 0 of Philox4x32-10 at the counter truncated
+//    to 32 bits, one generator call per rounded value (bit-identical to muon_sr).
+//  * SrNoise<NOISE_FAST> -- one generator call per 8 consecutive counters; counter c uses the
+//    16-bit half (c & 1) of word ((c >> 1) & 3) of Philox4x32-10 at counter (c >> 3)
+//    (64-bit). Same keys. Statistically an unbiased 16-bit uniform per value like the
+//    reference's, but different bits.
+//  * SrNoise<NOISE_NONE> -- no noise: round_bf16 rounds to nearest even instead.
 // ---------------------------------------------------------------------------------------
+enum NoiseMode : int { NOISE_REF = MSR_SR_NOISE_REFERENCE, NOISE_FAST = MSR_SR_NOISE_FAST, NOISE_NONE = MSR_SR_NOISE_NONE };
+
 __device__ __forceinline__ uint32_t half_of(uint4 w, uint32_t k) {
   const uint32_t word = k < 2 ? w.x : (k < 4 ? w.y : (k < 6 ? w.z : w.w));
   return (word >> (16u * (k & 1u))) & 0xFFFFu;
 }
 
-template <bool FAST>
+template <int MODE>
 struct SrNoise {
   PhiloxKey key;
 
   __device__ __forceinline__ uint32_t at(uint64_t ctr) const {
-    if (FAST) return half_of(philox4(ctr >> 3, key), static_cast<uint32_t>(ctr & 7u));
+    if (MODE == NOISE_NONE) return 0u;
+    if (MODE == NOISE_FAST) return half_of(philox4(ctr >> 3, key), static_cast<uint32_t>(ctr & 7u));
     return philox_word0(static_cast<uint32_t>(ctr), key);
   }
 
   // Noise for the 8 consecutive counters ctr0 .. ctr0 + 7 into r[0..7].
   __device__ __forceinline__ void eight(uint64_t ctr0, uint32_t* r) const {
-    if (!FAST) {
+    if (MODE == NOISE_NONE) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = 0u;
+      return;
+    }
+    if (MODE == NOISE_REF) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) r[j] = philox_word0(static_cast<uint32_t>(ctr0 + j), key);
       return;
@@ -142,6 +152,14 @@ __device__ __forceinline__ uint16_t sr_bf16_bits(float x, uint32_t rand) {
 
 __device__ __forceinline__ uint16_t rne_bf16_bits(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// The rounding of every SR store: stochastic with the mode's noise word, or round to
+// nearest even in NOISE_NONE (the noise word is then unused).
+template <int MODE>
+__device__ __forceinline__ uint16_t round_bf16(float x, uint32_t rand) {
+  if (MODE == NOISE_NONE) return rne_bf16_bits(x);
+  return sr_bf16_bits(x, rand);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -45,9 +45,10 @@ __global__ void philox_fill_kernel(uint32_t* out, int64_t n, uint64_t ctr_base, 
 // ---------------------------------------------------------------------------------------
 // SR gradient accumulation: acc <- SR(acc + g) -- muon_sr/triton_adamw.py:206-229
 // ---------------------------------------------------------------------------------------
+template <int NOISE>
 __device__ __forceinline__ uint16_t accum_one(uint16_t a, uint16_t g, uint32_t rnd) {
   const float s = fadd(bf16_bits_to_f32(a), bf16_bits_to_f32(g));
-  return sr_bf16_bits(s, rnd);
+  return round_bf16<NOISE>(s, rnd);
 }
 
 // First micro-batch: SR(0 + g) == g exactly (g is already bf16), except -0 + 0 = +0.
@@ -68,11 +69,12 @@ __global__ __launch_bounds__(EW_THREADS) void grad_accum_first_kernel(uint16_t* 
     acc[i] = first_one(g[i]);
 }
 
-template <bool VEC, bool FAST>
+template <bool VEC, int NOISE>
 __global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __restrict__ acc,
                                                                const uint16_t* __restrict__ g,
                                                                int64_t n, PhiloxKey key) {
-  const SrNoise<FAST> nz{key};
+  constexpr bool FAST = NOISE == NOISE_FAST;
+  const SrNoise<NOISE> nz{key};
   const int64_t nchunks = (n + EW_CHUNK - 1) / EW_CHUNK;
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
     const int64_t base = chunk * EW_CHUNK;
@@ -95,16 +97,17 @@ __global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __r
           if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            o.v[j] = accum_one(va[it].v[j], vg[it].v[j], FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
+            o.v[j] = accum_one<NOISE>(va[it].v[j], vg[it].v[j],
+                                      FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
           st_u16x8(acc + idx, o);
         } else {
-          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
+          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one<NOISE>(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
         }
       }
     } else {
       for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
-        if (i < n) acc[i] = accum_one(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
+        if (i < n) acc[i] = accum_one<NOISE>(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
       }
     }
   }
@@ -124,19 +127,20 @@ struct PrepareArgs {
 
 // `rnd()` yields the element's noise word; it is called after the math, where the noise is
 // consumed, which keeps the register allocation of the Philox chain as short as possible.
-template <class Rnd>
+template <int NOISE, class Rnd>
 __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, float beta, float omb, bool nesterov,
                                             Rnd rnd, uint16_t& buf_out, uint16_t& upd_out) {
   const float g = bf16_bits_to_f32(g_bits);
   const float buf = bf16_bits_to_f32(b_bits);
   const float nb = fadd(buf, fmul(omb, fsub(g, buf)));
   const float upd = nesterov ? fadd(g, fmul(beta, fsub(nb, g))) : nb;
-  buf_out = sr_bf16_bits(nb, rnd());
+  buf_out = round_bf16<NOISE>(nb, rnd());
   upd_out = rne_bf16_bits(upd);
 }
 
-template <bool FAST>
+template <int NOISE>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
   const int64_t total = a.prefix[a.count];
   const bool nesterov = a.nesterov != 0;
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
@@ -146,7 +150,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
     uint16_t* mb = static_cast<uint16_t*>(E.momentum);
     uint16_t* up = static_cast<uint16_t*>(E.update);
     const int64_t n = E.numel;
-    const SrNoise<FAST> nz{make_key(E.key)};
+    const SrNoise<NOISE> nz{make_key(E.key)};
     const uint64_t cb = E.ctr_base;
     const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
     if (a.vec[ei]) {
@@ -168,14 +172,15 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
           if (FAST) nz.eight(cb + static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            prepare_one(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
-                        [&] { return FAST ? r[j] : nz.at(cb + static_cast<uint64_t>(idx + j)); }, ob.v[j], ou.v[j]);
+            prepare_one<NOISE>(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
+                               [&] { return FAST ? r[j] : nz.at(cb + static_cast<uint64_t>(idx + j)); }, ob.v[j],
+                               ou.v[j]);
           st_u16x8(mb + idx, ob);
           st_u16x8(up + idx, ou);
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t ob, ou;
-            prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+            prepare_one<NOISE>(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
             mb[i] = ob;
             up[i] = ou;
           }
@@ -186,7 +191,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t ob, ou;
-          prepare_one(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+          prepare_one<NOISE>(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
           mb[i] = ob;
           up[i] = ou;
         }
@@ -206,16 +211,18 @@ struct ApplyArgs {
   float lr, decay;
 };
 
+template <int NOISE>
 __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, float scale, float lr, float decay,
                                               uint32_t rnd) {
   const float u = fmul(bf16_bits_to_f32(u_bits), scale);
   float p = fmul(bf16_bits_to_f32(p_bits), decay);
   p = fsub(p, fmul(lr, u));
-  return sr_bf16_bits(p, rnd);
+  return round_bf16<NOISE>(p, rnd);
 }
 
-template <bool FAST>
+template <int NOISE>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
@@ -223,7 +230,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* u = static_cast<const uint16_t*>(E.update);
     const int64_t n = E.numel;
-    const SrNoise<FAST> nz{make_key(E.key)};
+    const SrNoise<NOISE> nz{make_key(E.key)};
     const float scale = E.scale;
     const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
     if (a.vec[ei]) {
@@ -245,18 +252,18 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_
           if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            o.v[j] = apply_one(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay,
-                               FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
+            o.v[j] = apply_one<NOISE>(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay,
+                                      FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
           st_u16x8(p + idx, o);
         } else {
           for (int64_t i = idx; i < n; ++i)
-            p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
+            p[i] = apply_one<NOISE>(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
         }
       }
     } else {
       for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
-        if (i < n) p[i] = apply_one(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
+        if (i < n) p[i] = apply_one<NOISE>(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
       }
     }
   }
@@ -273,7 +280,7 @@ struct AdamWArgs {
   msr_adamw_hparams hp;
 };
 
-template <class Rnd>
+template <int NOISE, class Rnd>
 __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uint16_t& m_bits, uint16_t& v_bits,
                                           const msr_adamw_hparams& hp, float step_size, float bc2s, Rnd rnd) {
   const float g = bf16_bits_to_f32(g_bits);
@@ -285,14 +292,15 @@ __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uin
   const float denom = fadd(__fdiv_rn(__fsqrt_rn(v), bc2s), hp.eps);
   p = fmul(p, hp.decay);
   p = fsub(p, __fdiv_rn(fmul(step_size, m), denom));
-  m_bits = sr_bf16_bits(m, rnd(0));
-  v_bits = sr_bf16_bits(v, rnd(1));
-  p_bits = sr_bf16_bits(p, rnd(2));
+  m_bits = round_bf16<NOISE>(m, rnd(0));
+  v_bits = round_bf16<NOISE>(v, rnd(1));
+  p_bits = round_bf16<NOISE>(p, rnd(2));
 }
 
 // ITERS vectors of 8 elements per thread and chunk; MINB CTAs per SM for the register budget.
-template <int ITERS, int MINB, bool FAST>
+template <int ITERS, int MINB, int NOISE>
 __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
   constexpr int64_t CHUNK = EW_THREADS * EW_VEC * ITERS;
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
@@ -303,7 +311,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
     uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
     uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
     const int64_t n = E.numel;
-    const SrNoise<FAST> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
+    const SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
     const float ss = E.step_size, bc2s = E.bc2_sqrt;
     const int64_t base = (chunk - a.prefix[ei]) * CHUNK;
     if (a.vec[ei]) {
@@ -331,7 +339,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j) {
             const uint64_t c = static_cast<uint64_t>(idx + j);
-            adamw_one(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s, [&](int w) {
+            adamw_one<NOISE>(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s, [&](int w) {
               return w == 0 ? (FAST ? rm[j] : nm.at(c)) : w == 1 ? (FAST ? rv[j] : nv.at(c)) : (FAST ? rp[j] : np_.at(c));
             });
           }
@@ -341,7 +349,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t pb = p[i], mb = m[i], vb = v[i];
-            adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+            adamw_one<NOISE>(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
               const uint64_t c = static_cast<uint64_t>(i);
               return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
             });
@@ -354,7 +362,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t pb = p[i], mb = m[i], vb = v[i];
-          adamw_one(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+          adamw_one<NOISE>(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
               const uint64_t c = static_cast<uint64_t>(i);
               return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
             });
@@ -467,8 +475,10 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
           static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
     return check_launch("grad_accum_first_kernel");
   }
-  auto* kern = vec ? (sr_noise_fast() ? grad_accum_kernel<true, true> : grad_accum_kernel<true, false>)
-                  : (sr_noise_fast() ? grad_accum_kernel<false, true> : grad_accum_kernel<false, false>);
+  auto* kern = vec ? pick_noise(grad_accum_kernel<true, NOISE_REF>, grad_accum_kernel<true, NOISE_FAST>,
+                                grad_accum_kernel<true, NOISE_NONE>)
+                  : pick_noise(grad_accum_kernel<false, NOISE_REF>, grad_accum_kernel<false, NOISE_FAST>,
+                               grad_accum_kernel<false, NOISE_NONE>);
   kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(static_cast<uint16_t*>(acc),
                                                                static_cast<const uint16_t*>(grad), n, make_key(key));
   return check_launch("grad_accum_kernel");
@@ -497,7 +507,8 @@ int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, fl
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    auto* kern = sr_noise_fast() ? muon_prepare_kernel<true> : muon_prepare_kernel<false>;
+    auto* kern = pick_noise(muon_prepare_kernel<NOISE_REF>, muon_prepare_kernel<NOISE_FAST>,
+                            muon_prepare_kernel<NOISE_NONE>);
     kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("muon_prepare_kernel");
     if (st) return st;
@@ -525,7 +536,8 @@ int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float de
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    auto* kern = sr_noise_fast() ? muon_apply_kernel<true> : muon_apply_kernel<false>;
+    auto* kern = pick_noise(muon_apply_kernel<NOISE_REF>, muon_apply_kernel<NOISE_FAST>,
+                            muon_apply_kernel<NOISE_NONE>);
     kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("muon_apply_kernel");
     if (st) return st;
@@ -554,8 +566,9 @@ int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
     }
     a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    auto* kern = sr_noise_fast() ? adamw_kernel<ADAMW_ITERS, ADAMW_MINB, true>
-                                 : adamw_kernel<ADAMW_ITERS, ADAMW_MINB, false>;
+    auto* kern = pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF>,
+                            adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST>,
+                            adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE>);
     kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("adamw_kernel");
     if (st) return st;

@@ -12,7 +12,7 @@ static thread_local char t_last_error[512] = "";
 static std::atomic<uint64_t> g_launches{0};
 static std::atomic<int> g_sr_noise{MSR_SR_NOISE_REFERENCE};
 
-bool sr_noise_fast() { return g_sr_noise.load(std::memory_order_relaxed) == MSR_SR_NOISE_FAST; }
+int sr_noise_mode() { return g_sr_noise.load(std::memory_order_relaxed); }
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -57,7 +57,7 @@ extern "C" {
 int msr_abi_version(void) { return 1; }
 
 int msr_set_sr_noise(int mode) {
-  if (mode != MSR_SR_NOISE_REFERENCE && mode != MSR_SR_NOISE_FAST)
+  if (mode != MSR_SR_NOISE_REFERENCE && mode != MSR_SR_NOISE_FAST && mode != MSR_SR_NOISE_NONE)
     return msr::fail(MSR_ERR_INVALID, "msr_set_sr_noise: unknown mode %d", mode);
   msr::g_sr_noise.store(mode);
   return MSR_OK;

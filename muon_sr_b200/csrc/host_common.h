@@ -23,7 +23,17 @@ int require_sm100();
 
 inline cudaStream_t to_stream(msr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
-// Stochastic-rounding noise stream selected with msr_set_sr_noise (true: fast mode).
-bool sr_noise_fast();
+// Stochastic-rounding noise stream selected with msr_set_sr_noise (an msr_sr_noise value).
+int sr_noise_mode();
+
+// The kernel instance for the selected noise stream.
+template <class F>
+F pick_noise(F reference, F fast, F none) {
+  switch (sr_noise_mode()) {
+    case MSR_SR_NOISE_FAST: return fast;
+    case MSR_SR_NOISE_NONE: return none;
+    default: return reference;
+  }
+}
 
 }  // namespace msr

@@ -240,14 +240,16 @@ def centralize(grad: torch.Tensor, centralization: float) -> torch.Tensor:
     return out
 
 
-SR_NOISE_MODES = {"reference": 0, "fast": 1}
+SR_NOISE_MODES = {"reference": 0, "fast": 1, "none": 2}
 
 
 def set_sr_noise(mode: str = "reference") -> None:
     """Noise stream of every stochastic rounding (process-wide). ``"reference"`` (default):
     the reference's Philox stream, bit-identical results. ``"fast"``: one Philox4x32-10 call
     per 8 consecutive values (16 bits each) -- unbiased stochastic rounding at a fraction of
-    the integer work, with different bits than the reference (see ``msr_set_sr_noise``)."""
+    the integer work, with different bits than the reference. ``"none"``: no stochastic
+    rounding, every SR store rounds to nearest even (a parity mode for checking the updates'
+    fp32 arithmetic, not for training). See ``msr_set_sr_noise``."""
     if mode not in SR_NOISE_MODES:
         raise ValueError(f"sr noise mode must be one of {sorted(SR_NOISE_MODES)}, got {mode!r}")
     _lib.check(_lib.load().msr_set_sr_noise(SR_NOISE_MODES[mode]), "msr_set_sr_noise")

@@ -8,8 +8,9 @@ the reference's own code run under the Triton interpreter.
 """
 import numpy as np
 
-from .philox import sr_noise, triton_key
-from .sr import bf16_to_f32, sr_bf16
+from .elementwise import sr_round
+from .philox import triton_key
+from .sr import bf16_to_f32
 
 f32 = np.float32
 
@@ -98,7 +99,7 @@ def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2
     s1/s2 are bf16 bits (SR with seed + 1 / seed + 2). BC1 = 1 - b1**step and
     BC2 = 1 - b2**step come from the host in double and are passed as fp32 (:203).
     Returns (p, s1, s2, absmax1, absmax2) with the same dtypes as the inputs. ``noise``
-    selects the reference's noise stream or the engine's fast one.
+    selects the rounding (``elementwise.sr_round``).
     """
     n = p_bits.size
     bc1, bc2, lr32, b1, omb1, b2, omb2, eps32, decay = adamw8bit_coefficients(
@@ -121,7 +122,7 @@ def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2
         coef = f32(lr32 * sq_bc2 / bc1)
         upd = (p - coef * m / (np.sqrt(v) + sq_bc2 * eps32)).astype(f32)
         updated = (upd * decay).astype(f32)
-    rounded = sr_bf16(updated, sr_noise(triton_key(seed), n, 0, noise))
+    rounded = sr_round(updated, triton_key(seed), 0, noise)
     p_out = np.where(finite, rounded, p_bits.astype(np.uint16)).astype(np.uint16)
     if quantized:
         s1o = np.empty(n, np.uint8)
@@ -137,6 +138,6 @@ def adamw8bit(p_bits, g_bits, s1, s2, absmax1, absmax2, Q1, Q2, lr, beta1, beta2
             a1[b] = mm
             a2[b] = vm
         return p_out, s1o, s2o, a1, a2
-    m_sr = sr_bf16(m, sr_noise(triton_key(seed, 1), n, 0, noise))
-    v_sr = sr_bf16(v, sr_noise(triton_key(seed, 2), n, 0, noise))
+    m_sr = sr_round(m, triton_key(seed, 1), 0, noise)
+    v_sr = sr_round(v, triton_key(seed, 2), 0, noise)
     return p_out, m_sr, v_sr, absmax1, absmax2

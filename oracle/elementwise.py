@@ -26,14 +26,24 @@ def counters(n: int, ctr_base: int = 0) -> np.ndarray:
     return (np.arange(n, dtype=np.uint64) + np.uint64(ctr_base)) & np.uint64(0xFFFFFFFF)
 
 
+def sr_round(x, key64: int, ctr_base: int = 0, noise: str = "reference"):
+    """The rounding of an SR store: stochastic with the noise stream ``noise`` ("reference":
+    the reference's Philox words, "fast": the engine's opt-in stream) at counters
+    ctr_base, ctr_base + 1, ..., or, for ``noise="none"`` (the engine's parity mode without
+    noise), round to nearest even like a plain fp32 -> bf16 cast."""
+    x = np.asarray(x, dtype=f32)
+    if noise == "none":
+        return rne_bf16(x)
+    return sr_bf16(x, sr_noise(key64, x.size, ctr_base, noise))
+
+
 def grad_accum(acc_bits, grad_bits, seed: int, noise: str = "reference"):
     """``_grad_accum_kernel`` -- ``muon_sr/triton_adamw.py:206-229``: acc <- SR(acc + g).
-    ``noise`` selects the reference's noise stream or the engine's fast one."""
+    ``noise`` selects the rounding (``sr_round``)."""
     acc = bf16_to_f32(acc_bits)
     g = bf16_to_f32(grad_bits)
     s = (acc + g).astype(f32)
-    r = sr_noise(triton_key(seed), acc.size, 0, noise)
-    return sr_bf16(s, r)
+    return sr_round(s, triton_key(seed), 0, noise)
 
 
 def muon_prepare(g_bits, buf_bits, beta: float, nesterov: bool, seed: int, ctr_base: int = 0,
@@ -58,10 +68,10 @@ def muon_prepare(g_bits, buf_bits, beta: float, nesterov: bool, seed: int, ctr_b
         update = (g + f32(beta) * (new_buf - g)).astype(f32)
     else:
         update = new_buf
-    r = sr_noise(triton_key(seed), g.size, ctr_base, noise)
+    buf_bits = sr_round(new_buf, triton_key(seed), ctr_base, noise)
     if return_f32:
-        return sr_bf16(new_buf, r), rne_bf16(update), update
-    return sr_bf16(new_buf, r), rne_bf16(update)
+        return buf_bits, rne_bf16(update), update
+    return buf_bits, rne_bf16(update)
 
 
 def ns_scale(rows: int, cols: int) -> float:
@@ -78,8 +88,7 @@ def muon_apply(p_bits, upd_bits, lr: float, weight_decay: float, scale: float, s
     decay = f32(1.0 - lr * weight_decay)
     p = (p * decay).astype(f32)
     p = (p - f32(lr) * upd).astype(f32)
-    r = sr_noise(triton_key(seed), p.size, 0, noise)
-    return sr_bf16(p, r)
+    return sr_round(p, triton_key(seed), 0, noise)
 
 
 def adamw_coefficients(lr, beta1, beta2, eps, weight_decay, step):
@@ -109,7 +118,5 @@ def adamw_sr(p_bits, g_bits, m_bits, v_bits, lr, beta1, beta2, eps, weight_decay
     denom = (np.sqrt(v) / bc2s + eps).astype(f32)
     p = (p * decay).astype(f32)
     p = (p - step_size * m / denom).astype(f32)
-    rm = sr_noise(triton_key(seed, 0), p.size, 0, noise)
-    rv = sr_noise(triton_key(seed, 1), p.size, 0, noise)
-    rp = sr_noise(triton_key(seed, 2), p.size, 0, noise)
-    return sr_bf16(p, rp), sr_bf16(m, rm), sr_bf16(v, rv)
+    return (sr_round(p, triton_key(seed, 2), 0, noise), sr_round(m, triton_key(seed, 0), 0, noise),
+            sr_round(v, triton_key(seed, 1), 0, noise))

@@ -58,7 +58,9 @@ def test_more_argument_errors_without_gpu():
     it touches a device."""
     lib = _lib.load()
     assert lib.msr_set_sr_noise(7) == 1 and b"unknown mode" in lib.msr_last_error()
-    assert lib.msr_set_sr_noise(0) == 0
+    assert lib.msr_set_sr_noise(-1) == 1
+    for mode in (1, 2, 0):  # fast, none, back to the reference's stream
+        assert lib.msr_set_sr_noise(mode) == 0
     assert lib.msr_test_wait_timeout(0, None) == 1
     assert lib.msr_centralize_bf16(None, None, 4, 4, 0.5, None) == 1
     assert lib.msr_gemm_bf16(None, 0, None, 0, None, None, 1, 8, 8, 8, 1.0, 0.0, None, 0, 0, 0, None) == 1
