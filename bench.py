@@ -344,6 +344,39 @@ def run_ours(args, rank, world, local_rank):
                  "sr_accum_hbm_gbs": 6 * n_all / (acc_ms * 1e-3) / 1e9,
                  "adamw_sr_gpt2_ms": aw_ms,
                  "adamw_sr_gpt2_hbm_gbs": 14 * n_gpt2 / (aw_ms * 1e-3) / 1e9}
+        # configs[0] matrices + configs[1] vectors as one GPT-2-small hybrid step, eager and
+        # replayed from a StepGraph: a short step, where the host's launch work shows
+        from muon_sr_b200 import StepGraph
+        mats = [torch.nn.Parameter(torch.empty(s, dtype=torch.bfloat16, device=device).normal_(0, 0.02, generator=gg))
+                for _ in range(12) for s in ((768, 2304), (768, 768), (768, 3072), (3072, 768))]
+        for p in mats:
+            p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gg)
+        opt_h = TritonMuonSRWithAuxAdam([
+            dict(params=mats, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+            dict(params=gpt2, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
+        ], batch_ns=True)
+
+        def host_ms(fn, n=20):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            t1 = time.perf_counter()
+            torch.cuda.synchronize()
+            return (t1 - t0) * 1e3 / n
+
+        eager_ms = time_steps(opt_h.step, 20, 3, 1)
+        eager_host = host_ms(opt_h.step)
+        extra.update({"gpt2_hybrid_step_ms": eager_ms, "gpt2_hybrid_host_issue_ms": eager_host,
+                      "gpt2_hybrid_ns_tflops": sum(ns_flops(p.shape) for p in mats) / (eager_ms * 1e-3) / 1e12})
+        try:
+            sg = StepGraph(opt_h)
+            extra.update({"gpt2_hybrid_step_ms_graph": time_steps(sg.step, 20, 3, 1),
+                          "gpt2_hybrid_host_issue_ms_graph": host_ms(sg.step)})
+            del sg
+        except RuntimeError as exc:  # reported, not fatal: the headline does not use graphs
+            extra["gpt2_hybrid_graph_error"] = str(exc)[:300]
+        del opt_h, mats
         del opt_a, gpt2
         torch.cuda.empty_cache()
 

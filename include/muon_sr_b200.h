@@ -154,6 +154,41 @@ typedef struct msr_adamw_hparams {
 int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp,
                  msr_stream_t stream);
 
+/* ---- Replayable launches (CUDA graphs) -------------------------------------------------
+ * msr_muon_prepare_rec / msr_muon_apply_rec / msr_adamw_sr_rec launch the kernels of
+ * msr_muon_prepare / msr_muon_apply / msr_adamw_sr, but the kernels read the launch's
+ * scalars and its entry table from `record`, in device memory, instead of from the launch
+ * parameters. A record (16-byte aligned) is the header struct below directly followed by
+ * `count` entries. `entries` (host memory) must list the same tensors and sizes as the
+ * record: it splits and sizes the launch and is validated as in the plain calls. A CUDA graph
+ * captured around these calls replays with whatever the records hold when its kernels run,
+ * so a caller moves a captured optimizer step to the next step -- new keys, bias
+ * corrections, learning rates -- by rewriting the scalar fields of its records (e.g. with a
+ * host-to-device copy captured at the start of the graph), without capturing again. The
+ * pointers and sizes in a record must stay those of the capture. No counterpart in the
+ * reference (its Triton launches take every scalar as a launch argument). */
+typedef struct msr_prepare_record {
+  float beta, one_minus_beta;
+  int32_t nesterov;
+  int32_t count;       /* entries that follow */
+} msr_prepare_record;
+
+typedef struct msr_apply_record {
+  float lr, decay;
+  int32_t count;
+  int32_t reserved;
+} msr_apply_record;
+
+typedef struct msr_adamw_record {
+  msr_adamw_hparams hp;
+  int32_t count;
+  int32_t reserved;
+} msr_adamw_record;
+
+int msr_muon_prepare_rec(const msr_prepare_entry* entries, int count, const void* record, msr_stream_t stream);
+int msr_muon_apply_rec(const msr_apply_entry* entries, int count, const void* record, msr_stream_t stream);
+int msr_adamw_sr_rec(const msr_adamw_entry* entries, int count, const void* record, msr_stream_t stream);
+
 /* Gradient centralisation for TritonAdamW's `centralization` option: grad viewed as
  * [rows][cols] (rows = leading dim, or 1 for a vector), out = bf16_rne(g - c * mean_row)
  * with the row mean in fp32. One read of the gradient, one bf16 write (out must not

@@ -13,6 +13,7 @@ from .muon import MuonSR, MuonSRWithAuxAdam, TritonMuonSR, TritonMuonSRWithAuxAd
 from .kernels import set_sr_noise
 from .sharding import Sharder
 from .staging import HostStaging
+from .graph import StepGraph
 
 __all__ = [
     "SRAccumulator",
@@ -20,5 +21,5 @@ __all__ = [
     "TritonAdamW", "TritonSRAccumulator",
     "MuonSR", "MuonSRWithAuxAdam",
     "TritonMuonSR", "TritonMuonSRWithAuxAdam",
-    "Sharder", "HostStaging", "create_dynamic_map", "set_sr_noise",
+    "Sharder", "HostStaging", "StepGraph", "create_dynamic_map", "set_sr_noise",
 ]

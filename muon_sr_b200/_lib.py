@@ -40,6 +40,18 @@ class AdamWHparams(ctypes.Structure):
                 ("one_minus_beta2", c_float), ("eps", c_float), ("decay", c_float)]
 
 
+class PrepareRecord(ctypes.Structure):
+    _fields_ = [("beta", c_float), ("one_minus_beta", c_float), ("nesterov", c_int32), ("count", c_int32)]
+
+
+class ApplyRecord(ctypes.Structure):
+    _fields_ = [("lr", c_float), ("decay", c_float), ("count", c_int32), ("reserved", c_int32)]
+
+
+class AdamWRecord(ctypes.Structure):
+    _fields_ = [("hp", AdamWHparams), ("count", c_int32), ("reserved", c_int32)]
+
+
 class Adam8Entry(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("state1", c_void_p), ("state2", c_void_p),
                 ("absmax1", c_void_p), ("absmax2", c_void_p), ("numel", c_int64), ("key_p", c_uint64),
@@ -69,6 +81,9 @@ SIGNATURES = [
     ("msr_muon_prepare", c_int, [ctypes.POINTER(PrepareEntry), c_int, c_float, c_float, c_int, c_void_p]),
     ("msr_muon_apply", c_int, [ctypes.POINTER(ApplyEntry), c_int, c_float, c_float, c_void_p]),
     ("msr_adamw_sr", c_int, [ctypes.POINTER(AdamWEntry), c_int, ctypes.POINTER(AdamWHparams), c_void_p]),
+    ("msr_muon_prepare_rec", c_int, [ctypes.POINTER(PrepareEntry), c_int, c_void_p, c_void_p]),
+    ("msr_muon_apply_rec", c_int, [ctypes.POINTER(ApplyEntry), c_int, c_void_p, c_void_p]),
+    ("msr_adamw_sr_rec", c_int, [ctypes.POINTER(AdamWEntry), c_int, c_void_p, c_void_p]),
     ("msr_centralize_bf16", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     ("msr_adamw8bit", c_int, [ctypes.POINTER(Adam8Entry), c_int, c_void_p, c_void_p,
                               ctypes.POINTER(Adam8Hparams), c_void_p]),

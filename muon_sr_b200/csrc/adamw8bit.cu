@@ -390,14 +390,16 @@ extern "C" int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, cons
     return fail(MSR_ERR_INVALID, "msr_adamw8bit: block_size %d is not a power of two in [32, 4096]", bs);
   const int ept = bs > 2048 ? 16 : 8;
   const int64_t tile = static_cast<int64_t>(Q_THREADS) * ept;
-  for (int start = 0; start < count; start += Q_MAXE) {
+  int next = 0;  // each group resumes at the first entry the previous one did not take
+  while (next < count) {
     Adam8Args a{};
     a.hp = *hp;
     a.qmap1 = qmap1;
     a.qmap2 = qmap2;
     int64_t tiles = 0;
     bool any_quant = false;
-    for (int i = start; i < count && a.count < Q_MAXE; ++i) {
+    int i = next;
+    for (; i < count && a.count < Q_MAXE; ++i) {
       const msr_adamw8bit_entry& e = entries[i];
       if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.grad || !e.state1 || !e.state2)))
         return fail(MSR_ERR_INVALID, "msr_adamw8bit: entry %d has a null pointer or negative numel", i);
@@ -412,6 +414,7 @@ extern "C" int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, cons
       tiles += (e.numel + tile - 1) / tile;
       ++a.count;
     }
+    next = i;
     a.prefix[a.count] = tiles;
     if (a.count == 0) continue;
     if (any_quant && (qmap1 == nullptr || qmap2 == nullptr))

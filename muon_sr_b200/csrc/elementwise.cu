@@ -123,7 +123,22 @@ struct PrepareArgs {
   int count;
   float beta, omb;
   int nesterov;
+  // Replayable launches (msr_muon_prepare_rec): scalars and entries come from this device
+  // record; src[i] is the record's index of entry i.
+  const msr_prepare_record* rec;
+  int32_t src[MAXE];
 };
+
+// Launch scalars and entry i of a launch, from the parameters or (REC) the device record.
+template <bool REC>
+__device__ __forceinline__ const msr_prepare_entry& entry_of(const PrepareArgs& a, int i) {
+  if constexpr (REC) return reinterpret_cast<const msr_prepare_entry*>(a.rec + 1)[a.src[i]];
+  else return a.e[i];
+}
+template <bool REC>
+__device__ __forceinline__ float beta_of(const PrepareArgs& a) { return REC ? a.rec->beta : a.beta; }
+template <bool REC>
+__device__ __forceinline__ float omb_of(const PrepareArgs& a) { return REC ? a.rec->one_minus_beta : a.omb; }
 
 // `rnd()` yields the element's noise word; it is called after the math, where the noise is
 // consumed, which keeps the register allocation of the Philox chain as short as possible.
@@ -138,14 +153,14 @@ __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, fl
   upd_out = rne_bf16_bits(upd);
 }
 
-template <int NOISE>
+template <int NOISE, bool REC>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
   constexpr bool FAST = NOISE == NOISE_FAST;
   const int64_t total = a.prefix[a.count];
-  const bool nesterov = a.nesterov != 0;
+  const bool nesterov = (REC ? a.rec->nesterov : a.nesterov) != 0;
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
-    const msr_prepare_entry& E = a.e[ei];
+    const msr_prepare_entry& E = entry_of<REC>(a, ei);
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* mb = static_cast<uint16_t*>(E.momentum);
     uint16_t* up = static_cast<uint16_t*>(E.update);
@@ -172,7 +187,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
           if (FAST) nz.eight(cb + static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            prepare_one<NOISE>(vg[it].v[j], vb[it].v[j], a.beta, a.omb, nesterov,
+            prepare_one<NOISE>(vg[it].v[j], vb[it].v[j], beta_of<REC>(a), omb_of<REC>(a), nesterov,
                                [&] { return FAST ? r[j] : nz.at(cb + static_cast<uint64_t>(idx + j)); }, ob.v[j],
                                ou.v[j]);
           st_u16x8(mb + idx, ob);
@@ -180,7 +195,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t ob, ou;
-            prepare_one<NOISE>(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+            prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
             mb[i] = ob;
             up[i] = ou;
           }
@@ -191,7 +206,7 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __gri
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t ob, ou;
-          prepare_one<NOISE>(g[i], mb[i], a.beta, a.omb, nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+          prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
           mb[i] = ob;
           up[i] = ou;
         }
@@ -209,7 +224,19 @@ struct ApplyArgs {
   uint8_t vec[MAXE];
   int count;
   float lr, decay;
+  const msr_apply_record* rec;  // msr_muon_apply_rec (see PrepareArgs)
+  int32_t src[MAXE];
 };
+
+template <bool REC>
+__device__ __forceinline__ const msr_apply_entry& entry_of(const ApplyArgs& a, int i) {
+  if constexpr (REC) return reinterpret_cast<const msr_apply_entry*>(a.rec + 1)[a.src[i]];
+  else return a.e[i];
+}
+template <bool REC>
+__device__ __forceinline__ float lr_of(const ApplyArgs& a) { return REC ? a.rec->lr : a.lr; }
+template <bool REC>
+__device__ __forceinline__ float decay_of(const ApplyArgs& a) { return REC ? a.rec->decay : a.decay; }
 
 template <int NOISE>
 __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, float scale, float lr, float decay,
@@ -220,13 +247,13 @@ __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, 
   return round_bf16<NOISE>(p, rnd);
 }
 
-template <int NOISE>
+template <int NOISE, bool REC>
 __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
   constexpr bool FAST = NOISE == NOISE_FAST;
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
-    const msr_apply_entry& E = a.e[ei];
+    const msr_apply_entry& E = entry_of<REC>(a, ei);
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* u = static_cast<const uint16_t*>(E.update);
     const int64_t n = E.numel;
@@ -252,18 +279,18 @@ __global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_
           if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j)
-            o.v[j] = apply_one<NOISE>(vp[it].v[j], vu[it].v[j], scale, a.lr, a.decay,
+            o.v[j] = apply_one<NOISE>(vp[it].v[j], vu[it].v[j], scale, lr_of<REC>(a), decay_of<REC>(a),
                                       FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
           st_u16x8(p + idx, o);
         } else {
           for (int64_t i = idx; i < n; ++i)
-            p[i] = apply_one<NOISE>(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
+            p[i] = apply_one<NOISE>(p[i], u[i], scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
         }
       }
     } else {
       for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
-        if (i < n) p[i] = apply_one<NOISE>(p[i], u[i], scale, a.lr, a.decay, nz.at(static_cast<uint64_t>(i)));
+        if (i < n) p[i] = apply_one<NOISE>(p[i], u[i], scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
       }
     }
   }
@@ -278,7 +305,20 @@ struct AdamWArgs {
   uint8_t vec[MAXE];
   int count;
   msr_adamw_hparams hp;
+  const msr_adamw_record* rec;  // msr_adamw_sr_rec (see PrepareArgs)
+  int32_t src[MAXE];
 };
+
+template <bool REC>
+__device__ __forceinline__ const msr_adamw_entry& entry_of(const AdamWArgs& a, int i) {
+  if constexpr (REC) return reinterpret_cast<const msr_adamw_entry*>(a.rec + 1)[a.src[i]];
+  else return a.e[i];
+}
+template <bool REC>
+__device__ __forceinline__ const msr_adamw_hparams& hp_of(const AdamWArgs& a) {
+  if constexpr (REC) return a.rec->hp;
+  else return a.hp;
+}
 
 template <int NOISE, class Rnd>
 __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uint16_t& m_bits, uint16_t& v_bits,
@@ -298,14 +338,14 @@ __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uin
 }
 
 // ITERS vectors of 8 elements per thread and chunk; MINB CTAs per SM for the register budget.
-template <int ITERS, int MINB, int NOISE>
+template <int ITERS, int MINB, int NOISE, bool REC>
 __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
   constexpr bool FAST = NOISE == NOISE_FAST;
   constexpr int64_t CHUNK = EW_THREADS * EW_VEC * ITERS;
   const int64_t total = a.prefix[a.count];
   for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
-    const msr_adamw_entry& E = a.e[ei];
+    const msr_adamw_entry& E = entry_of<REC>(a, ei);
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
@@ -339,7 +379,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
 #pragma unroll
           for (int j = 0; j < EW_VEC; ++j) {
             const uint64_t c = static_cast<uint64_t>(idx + j);
-            adamw_one<NOISE>(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], a.hp, ss, bc2s, [&](int w) {
+            adamw_one<NOISE>(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], hp_of<REC>(a), ss, bc2s, [&](int w) {
               return w == 0 ? (FAST ? rm[j] : nm.at(c)) : w == 1 ? (FAST ? rv[j] : nv.at(c)) : (FAST ? rp[j] : np_.at(c));
             });
           }
@@ -349,7 +389,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
         } else {
           for (int64_t i = idx; i < n; ++i) {
             uint16_t pb = p[i], mb = m[i], vb = v[i];
-            adamw_one<NOISE>(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+            adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), ss, bc2s, [&](int w) {
               const uint64_t c = static_cast<uint64_t>(i);
               return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
             });
@@ -362,7 +402,7 @@ __global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_co
         const int64_t i = base + it * EW_THREADS + threadIdx.x;
         if (i < n) {
           uint16_t pb = p[i], mb = m[i], vb = v[i];
-          adamw_one<NOISE>(pb, g[i], mb, vb, a.hp, ss, bc2s, [&](int w) {
+          adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), ss, bc2s, [&](int w) {
               const uint64_t c = static_cast<uint64_t>(i);
               return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
             });
@@ -431,6 +471,126 @@ inline int grid_for(int64_t chunks) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(chunks, cap)));
 }
 
+inline bool record_ok(const void* rec) { return rec != nullptr && (reinterpret_cast<uintptr_t>(rec) & 15u) == 0; }
+
+// The multi-tensor launchers: entries are packed MAXE at a time (empty ones skipped, each
+// group resuming at the first entry the previous one did not take); with a record, the
+// kernels take scalars and entries from it (src[] maps packed to record indices).
+int prepare_launch(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta, int nesterov,
+                   const msr_prepare_record* rec, msr_stream_t stream) {
+  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_prepare: bad entry list");
+  int next = 0;
+  while (next < count) {
+    PrepareArgs a{};
+    a.beta = beta;
+    a.omb = one_minus_beta;
+    a.nesterov = nesterov;
+    a.rec = rec;
+    int64_t chunks = 0;
+    int i = next;
+    for (; i < count && a.count < MAXE; ++i) {
+      const msr_prepare_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.grad || !e.momentum || !e.update)))
+        return fail(MSR_ERR_INVALID, "msr_muon_prepare: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.src[a.count] = i;
+      a.vec[a.count] = ptr_aligned16(e.grad) && ptr_aligned16(e.momentum) && ptr_aligned16(e.update);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
+      ++a.count;
+    }
+    next = i;
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    auto* kern = rec ? pick_noise(muon_prepare_kernel<NOISE_REF, true>, muon_prepare_kernel<NOISE_FAST, true>,
+                                  muon_prepare_kernel<NOISE_NONE, true>)
+                     : pick_noise(muon_prepare_kernel<NOISE_REF, false>, muon_prepare_kernel<NOISE_FAST, false>,
+                                  muon_prepare_kernel<NOISE_NONE, false>);
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_prepare_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
+int apply_launch(const msr_apply_entry* entries, int count, float lr, float decay, const msr_apply_record* rec,
+                 msr_stream_t stream) {
+  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_apply: bad entry list");
+  int next = 0;
+  while (next < count) {
+    ApplyArgs a{};
+    a.lr = lr;
+    a.decay = decay;
+    a.rec = rec;
+    int64_t chunks = 0;
+    int i = next;
+    for (; i < count && a.count < MAXE; ++i) {
+      const msr_apply_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.update)))
+        return fail(MSR_ERR_INVALID, "msr_muon_apply: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.src[a.count] = i;
+      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.update);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
+      ++a.count;
+    }
+    next = i;
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    auto* kern = rec ? pick_noise(muon_apply_kernel<NOISE_REF, true>, muon_apply_kernel<NOISE_FAST, true>,
+                                  muon_apply_kernel<NOISE_NONE, true>)
+                     : pick_noise(muon_apply_kernel<NOISE_REF, false>, muon_apply_kernel<NOISE_FAST, false>,
+                                  muon_apply_kernel<NOISE_NONE, false>);
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_apply_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
+int adamw_launch(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp, const msr_adamw_record* rec,
+                 msr_stream_t stream) {
+  if (count < 0 || (count > 0 && entries == nullptr))
+    return fail(MSR_ERR_INVALID, "msr_adamw_sr: bad entry list or hparams");
+  int next = 0;
+  while (next < count) {
+    AdamWArgs a{};
+    if (hp) a.hp = *hp;
+    a.rec = rec;
+    int64_t chunks = 0;
+    int i = next;
+    for (; i < count && a.count < MAXE; ++i) {
+      const msr_adamw_entry& e = entries[i];
+      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.grad || !e.exp_avg || !e.exp_avg_sq)))
+        return fail(MSR_ERR_INVALID, "msr_adamw_sr: entry %d has a null pointer or negative numel", i);
+      if (e.numel == 0) continue;
+      a.e[a.count] = e;
+      a.src[a.count] = i;
+      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.grad) && ptr_aligned16(e.exp_avg) &&
+                       ptr_aligned16(e.exp_avg_sq);
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + ADAMW_CHUNK - 1) / ADAMW_CHUNK;
+      ++a.count;
+    }
+    next = i;
+    a.prefix[a.count] = chunks;
+    if (a.count == 0) continue;
+    auto* kern = rec ? pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF, true>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST, true>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE, true>)
+                     : pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF, false>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST, false>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE, false>);
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("adamw_kernel");
+    if (st) return st;
+  }
+  return MSR_OK;
+}
+
 }  // namespace
 }  // namespace msr
 
@@ -486,94 +646,31 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
 
 int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta, int nesterov,
                      msr_stream_t stream) {
-  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_prepare: bad entry list");
-  for (int start = 0; start < count; start += MAXE) {
-    PrepareArgs a{};
-    a.count = 0;
-    a.beta = beta;
-    a.omb = one_minus_beta;
-    a.nesterov = nesterov;
-    int64_t chunks = 0;
-    for (int i = start; i < count && a.count < MAXE; ++i) {
-      const msr_prepare_entry& e = entries[i];
-      if (e.numel < 0 || (e.numel > 0 && (!e.grad || !e.momentum || !e.update)))
-        return fail(MSR_ERR_INVALID, "msr_muon_prepare: entry %d has a null pointer or negative numel", i);
-      if (e.numel == 0) continue;
-      a.e[a.count] = e;
-      a.vec[a.count] = ptr_aligned16(e.grad) && ptr_aligned16(e.momentum) && ptr_aligned16(e.update);
-      a.prefix[a.count] = chunks;
-      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
-      ++a.count;
-    }
-    a.prefix[a.count] = chunks;
-    if (a.count == 0) continue;
-    auto* kern = pick_noise(muon_prepare_kernel<NOISE_REF>, muon_prepare_kernel<NOISE_FAST>,
-                            muon_prepare_kernel<NOISE_NONE>);
-    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
-    int st = check_launch("muon_prepare_kernel");
-    if (st) return st;
-  }
-  return MSR_OK;
+  return msr::prepare_launch(entries, count, beta, one_minus_beta, nesterov, nullptr, stream);
+}
+
+int msr_muon_prepare_rec(const msr_prepare_entry* entries, int count, const void* record, msr_stream_t stream) {
+  if (!msr::record_ok(record)) return fail(MSR_ERR_INVALID, "msr_muon_prepare_rec: record must be 16-byte aligned");
+  return msr::prepare_launch(entries, count, 0.f, 0.f, 0, static_cast<const msr_prepare_record*>(record), stream);
 }
 
 int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float decay, msr_stream_t stream) {
-  if (count < 0 || (count > 0 && entries == nullptr)) return fail(MSR_ERR_INVALID, "msr_muon_apply: bad entry list");
-  for (int start = 0; start < count; start += MAXE) {
-    ApplyArgs a{};
-    a.lr = lr;
-    a.decay = decay;
-    int64_t chunks = 0;
-    for (int i = start; i < count && a.count < MAXE; ++i) {
-      const msr_apply_entry& e = entries[i];
-      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.update)))
-        return fail(MSR_ERR_INVALID, "msr_muon_apply: entry %d has a null pointer or negative numel", i);
-      if (e.numel == 0) continue;
-      a.e[a.count] = e;
-      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.update);
-      a.prefix[a.count] = chunks;
-      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
-      ++a.count;
-    }
-    a.prefix[a.count] = chunks;
-    if (a.count == 0) continue;
-    auto* kern = pick_noise(muon_apply_kernel<NOISE_REF>, muon_apply_kernel<NOISE_FAST>,
-                            muon_apply_kernel<NOISE_NONE>);
-    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
-    int st = check_launch("muon_apply_kernel");
-    if (st) return st;
-  }
-  return MSR_OK;
+  return msr::apply_launch(entries, count, lr, decay, nullptr, stream);
+}
+
+int msr_muon_apply_rec(const msr_apply_entry* entries, int count, const void* record, msr_stream_t stream) {
+  if (!msr::record_ok(record)) return fail(MSR_ERR_INVALID, "msr_muon_apply_rec: record must be 16-byte aligned");
+  return msr::apply_launch(entries, count, 0.f, 0.f, static_cast<const msr_apply_record*>(record), stream);
 }
 
 int msr_adamw_sr(const msr_adamw_entry* entries, int count, const msr_adamw_hparams* hp, msr_stream_t stream) {
-  if (count < 0 || (count > 0 && (entries == nullptr || hp == nullptr)))
-    return fail(MSR_ERR_INVALID, "msr_adamw_sr: bad entry list or hparams");
-  for (int start = 0; start < count; start += MAXE) {
-    AdamWArgs a{};
-    a.hp = *hp;
-    int64_t chunks = 0;
-    for (int i = start; i < count && a.count < MAXE; ++i) {
-      const msr_adamw_entry& e = entries[i];
-      if (e.numel < 0 || (e.numel > 0 && (!e.param || !e.grad || !e.exp_avg || !e.exp_avg_sq)))
-        return fail(MSR_ERR_INVALID, "msr_adamw_sr: entry %d has a null pointer or negative numel", i);
-      if (e.numel == 0) continue;
-      a.e[a.count] = e;
-      a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.grad) && ptr_aligned16(e.exp_avg) &&
-                       ptr_aligned16(e.exp_avg_sq);
-      a.prefix[a.count] = chunks;
-      chunks += (e.numel + ADAMW_CHUNK - 1) / ADAMW_CHUNK;
-      ++a.count;
-    }
-    a.prefix[a.count] = chunks;
-    if (a.count == 0) continue;
-    auto* kern = pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF>,
-                            adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST>,
-                            adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE>);
-    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
-    int st = check_launch("adamw_kernel");
-    if (st) return st;
-  }
-  return MSR_OK;
+  if (count > 0 && hp == nullptr) return fail(MSR_ERR_INVALID, "msr_adamw_sr: bad entry list or hparams");
+  return msr::adamw_launch(entries, count, hp, nullptr, stream);
+}
+
+int msr_adamw_sr_rec(const msr_adamw_entry* entries, int count, const void* record, msr_stream_t stream) {
+  if (!msr::record_ok(record)) return fail(MSR_ERR_INVALID, "msr_adamw_sr_rec: record must be 16-byte aligned");
+  return msr::adamw_launch(entries, count, nullptr, static_cast<const msr_adamw_record*>(record), stream);
 }
 
 }  // extern "C"

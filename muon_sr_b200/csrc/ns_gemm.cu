@@ -714,11 +714,30 @@ size_t smem_bytes() { return sizeof(SharedStorage) + 1024; }
 
 std::atomic<int> g_gemm_max_ctas{0};
 
+constexpr int MAX_DEVICES = 64;
+
+// Sets a kernel's dynamic shared memory limit once per device (slot: one per kernel
+// variant), so that launches after the first -- e.g. inside a CUDA graph capture -- make
+// no attribute call.
+template <class K>
+int smem_attr_once(K kern, int smem, std::atomic<int>* done_per_device) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>& done = done_per_device[dev % MAX_DEVICES];
+  if (done.load(std::memory_order_acquire)) return MSR_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  done.store(1, std::memory_order_release);
+  return MSR_OK;
+}
+
+std::atomic<int> g_single_attr[4][MAX_DEVICES];
+std::atomic<int> g_pair_attr[4][MAX_DEVICES];
+
 template <int A_MN, int B_MN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
   auto kern = gemm_kernel<A_MN, B_MN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes());
-  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_attr_once(kern, (int)smem_bytes(), g_single_attr[A_MN * 2 + B_MN])) return st;
   int ctas = sm_count();
   const int cap = g_gemm_max_ctas.load(std::memory_order_relaxed);
   if (cap > 0 && cap < ctas) ctas = cap;
@@ -733,15 +752,14 @@ std::atomic<int> g_gemm_pairs{1};
 
 // Clusters of two that fit on the device at once (a GPC with an odd number of free SMs
 // leaves one idle), per kernel variant and device.
-constexpr int MAX_DEVICES = 64;
 std::atomic<int> g_pair_capacity[4][MAX_DEVICES];
 
 template <int A_MN, int B_MN>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
   auto kern = gemm_pair_kernel<A_MN, B_MN>;
   const int smem = static_cast<int>(pair_smem_bytes());
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (int st = smem_attr_once(kern, smem, g_pair_attr[A_MN * 2 + B_MN])) return st;
+  cudaError_t e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;

@@ -34,6 +34,17 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
+# Set by ``graph.StepGraph`` while it sizes, captures or refreshes a step: the multi-tensor
+# launches below then go through it (replayable launches whose scalars live in a device
+# record), and in its passes that issue no kernels (``recorder.launches`` False) the
+# Newton-Schulz and centralisation calls return without launching.
+_recorder = None
+
+
+def _issuing():
+    return _recorder is None or _recorder.launches
+
+
 # ---------------------------------------------------------------------------------------
 def philox_fill(n: int, ctr_base: int, key: int, device) -> torch.Tensor:
     """Test hook: Philox words for counters ctr_base .. ctr_base + n - 1 (as int32)."""
@@ -68,6 +79,10 @@ def muon_prepare(items, beta: float, nesterov: bool) -> None:
         e.ctr_base = ctr_base & 0xFFFFFFFFFFFFFFFF
         e.key = triton_key(seed)
     dev = items[0][0].device
+    if _recorder is not None:
+        hdr = _lib.PrepareRecord(float(f32(beta)), float(f32(1.0 - beta)), int(bool(nesterov)), len(items))
+        _recorder.launch("msr_muon_prepare_rec", hdr, arr, dev)
+        return
     _lib.check(_lib.load().msr_muon_prepare(arr, len(items), float(f32(beta)), float(f32(1.0 - beta)),
                                             int(bool(nesterov)), stream_handle(dev)), "msr_muon_prepare")
 
@@ -85,6 +100,10 @@ def muon_apply(items, lr: float, weight_decay: float) -> None:
         e.key = triton_key(seed)
         e.scale = float(f32(scale))
     dev = items[0][0].device
+    if _recorder is not None:
+        hdr = _lib.ApplyRecord(float(f32(lr)), float(f32(1.0 - lr * weight_decay)), len(items), 0)
+        _recorder.launch("msr_muon_apply_rec", hdr, arr, dev)
+        return
     _lib.check(_lib.load().msr_muon_apply(arr, len(items), float(f32(lr)), float(f32(1.0 - lr * weight_decay)),
                                           stream_handle(dev)), "msr_muon_apply")
 
@@ -106,6 +125,9 @@ def adamw_sr(items, lr: float, beta1: float, beta2: float, eps: float, weight_de
     hp = _lib.AdamWHparams(float(f32(beta1)), float(f32(1.0 - beta1)), float(f32(beta2)), float(f32(1.0 - beta2)),
                            float(f32(eps)), float(f32(1.0 - lr * weight_decay)))
     dev = items[0][0].device
+    if _recorder is not None:
+        _recorder.launch("msr_adamw_sr_rec", _lib.AdamWRecord(hp, len(items), 0), arr, dev)
+        return
     _lib.check(_lib.load().msr_adamw_sr(arr, len(items), ctypes.byref(hp), stream_handle(dev)), "msr_adamw_sr")
 
 
@@ -128,6 +150,8 @@ def quant_tables(qmap1: torch.Tensor, qmap2: torch.Tensor):
 def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_size, qtables=None) -> None:
     """items: iterable of (param, grad, state1, state2, absmax1, absmax2, step, seed, quantized).
     ``qtables``: the lookup-table blob of ``quant_tables`` (None runs the codebook walk)."""
+    if _recorder is not None:
+        raise RuntimeError("8-bit AdamW launches cannot be captured in a StepGraph")
     items = list(items)
     if not items:
         return
@@ -189,6 +213,8 @@ def newton_schulz(x: torch.Tensor, steps: int = 5, norm_sq: torch.Tensor = None,
         raise ValueError("Newton-Schulz needs a tensor with ndim >= 2")
     rows, cols = x.shape[-2], x.shape[-1]
     batch = x.numel() // max(1, rows * cols)
+    if not _issuing():
+        return x if out is None else out  # a refresh pass: the captured graph computes it
     if out is None:
         out = torch.empty_like(x)
     if batch == 0:
@@ -228,6 +254,10 @@ def centralize(grad: torch.Tensor, centralization: float) -> torch.Tensor:
     """``bf16(g - c * g.mean(dim=trailing dims, keepdim=True))`` with the mean in fp32, as
     TritonAdamW's centralization (muon_sr/triton_adamw.py:179-187), in one fused kernel;
     returns a new bf16 tensor."""
+    if _recorder is not None:
+        _recorder.constant("centralization", float(centralization))
+        if not _recorder.launches:
+            return grad
     g = grad if grad.is_contiguous() else grad.contiguous()
     _require(g, "grad")
     out = torch.empty_like(g, memory_format=torch.contiguous_format)

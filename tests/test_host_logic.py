@@ -357,3 +357,62 @@ def test_staging_batches():
         S._tls.io = None
     assert got == [[1 << 27, 1 << 27], [1 << 27], [1 << 29], [5]]
     assert [x for b in got for x in b] == items
+
+
+def test_step_graph_record_refresh():
+    """A refresh rewrites a captured record's scalars (header and per-entry keys / scales)
+    but keeps the captured pointers, and refuses a launch whose structure differs."""
+    from muon_sr_b200 import _lib
+    from muon_sr_b200 import graph as G
+    m = G._Recorder("measure")
+    arr = (_lib.ApplyEntry * 2)()
+    arr[0].numel, arr[1].numel = 10, 20
+    m.launch("msr_muon_apply_rec", _lib.ApplyRecord(0.5, 0.9, 2, 0), arr, None)
+    assert m.size == 16 + 2 * 40 and len(m.plan) == 1
+    host = torch.zeros(m.size, dtype=torch.uint8)
+    cap = (_lib.ApplyEntry * 2)()
+    cap[0].param, cap[0].update, cap[0].numel = 0x1000, 0x3000, 10
+    cap[1].param, cap[1].update, cap[1].numel = 0x2000, 0x4000, 20
+    plan = [G._Launch("msr_muon_apply_rec", 0, _lib.ApplyRecord(0.0, 0.0, 2, 0), cap)]
+    new = (_lib.ApplyEntry * 2)()
+    new[0].param, new[0].numel, new[0].key, new[0].scale = 0xDEAD, 10, 7, 1.5
+    new[1].param, new[1].numel, new[1].key, new[1].scale = 0xBEEF, 20, 8, 2.0
+    r = G._Recorder("refresh", host, None, plan=plan, constants=[])
+    r.launch("msr_muon_apply_rec", _lib.ApplyRecord(0.25, 0.99, 2, 0), new, None)
+    assert r.complete()
+    raw = host.numpy().tobytes()
+    hdr = _lib.ApplyRecord.from_buffer_copy(raw[:16])
+    ents = (_lib.ApplyEntry * 2).from_buffer_copy(raw[16:96])
+    assert (hdr.lr, hdr.count) == (0.25, 2)
+    assert [(e.param, e.update, e.numel, e.key, e.scale) for e in ents] == \
+        [(0x1000, 0x3000, 10, 7, 1.5), (0x2000, 0x4000, 20, 8, 2.0)]
+    bad = (_lib.ApplyEntry * 1)()
+    bad[0].numel = 10
+    with pytest.raises(RuntimeError, match="captured graph"):
+        G._Recorder("refresh", host, None, plan=plan, constants=[]).launch(
+            "msr_muon_apply_rec", _lib.ApplyRecord(0.25, 0.99, 1, 0), bad, None)
+    c = G._Recorder("refresh", host, None, plan=[], constants=[("centralization", 0.5)])
+    with pytest.raises(RuntimeError, match="captured graph"):
+        c.constant("centralization", 0.25)
+
+
+def test_step_graph_snapshot_restore():
+    """Passes that size or capture a step leave step counters, the global step and torch's
+    generator as they found them; tensors in the state are the same objects."""
+    from muon_sr_b200 import TritonMuonSR
+    from muon_sr_b200 import graph as G
+    p = torch.nn.Parameter(torch.zeros(4, 4, dtype=torch.bfloat16))
+    opt = TritonMuonSR([p], batch_ns=True)
+    buf = torch.zeros(4, 4, dtype=torch.bfloat16)
+    opt.state[p].update(step=3, momentum_buffer=buf)
+    opt._clock.value = 3
+    snap = G._snapshot(opt)
+    draw = torch.randint(0, 1 << 30, (1,)).item()
+    opt.state[p]["step"] = 4
+    opt.state[p]["extra"] = 1
+    opt._clock.value = 4
+    torch.randint(0, 1 << 30, (1,))
+    G._restore(opt, snap)
+    assert opt.state[p]["step"] == 3 and "extra" not in opt.state[p]
+    assert opt.state[p]["momentum_buffer"] is buf and opt._clock.value == 3
+    assert torch.randint(0, 1 << 30, (1,)).item() == draw

@@ -236,18 +236,25 @@ def test_sr_statistics_256_seeds():
 def test_centralize_matches_reference_ops(shape):
     """The fused centralisation kernel against the reference's torch ops
     (muon_sr/triton_adamw.py:179-187) on the same GPU: bf16(g - c * mean_row) with the mean in
-    fp32. Only the fp32 mean's summation order differs, so an element may differ by one bf16
-    ulp, on a small fraction of elements."""
-    g = (torch.randn(*shape, device="cuda") * 1e-3).bfloat16()
+    fp32. Only the fp32 mean's summation order differs (a few fp32 ulps of the row's mean), so
+    an element may differ by one bf16 ulp of the result plus that difference -- which is
+    several bf16 ulps where g - c * mean nearly cancels -- on a small fraction of elements."""
+    gen = torch.Generator(device="cuda").manual_seed(sum(shape))
+    g = (torch.randn(*shape, device="cuda", generator=gen) * 1e-3).bfloat16()
     g[..., 0] += 5e-3  # rows with a clear nonzero mean
     g0 = g.clone()
     got = K.centralize(g, 0.5)
+    dims = tuple(range(1, g.dim()))
     g32 = g.to(torch.float32)
-    g32.sub_(g32.mean(dim=tuple(range(1, g32.dim())), keepdim=True).mul_(0.5))
+    g32.sub_(g32.mean(dim=dims, keepdim=True).mul_(0.5))
     want = g32.to(torch.bfloat16)
     gi = got.view(torch.int16).int()
     wi = want.view(torch.int16).int()
     diff = (gi - wi).abs()
-    assert int(diff.max()) <= 1
     assert float((diff > 0).float().mean()) < 0.02
+    wf = want.float()
+    ulp = ((wi + 1).to(torch.int16).view(torch.bfloat16).float() - wf).abs()
+    row_mag = g.float().abs().mean(dim=dims, keepdim=True) if dims else g.float().abs().mean()
+    bound = ulp + 0.5 * 2.0 ** -18 * row_mag
+    assert bool(((got.float() - wf).abs() <= bound).all())
     assert torch.equal(g, g0)  # the gradient itself is not modified
