@@ -357,13 +357,15 @@ def run_ours(args, rank, world, local_rank):
         ], batch_ns=True)
 
         def host_ms(fn, n=20):
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
+            """Host time to issue one step, each call made with the GPU idle (no back-pressure)."""
+            total = 0.0
             for _ in range(n):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
                 fn()
-            t1 = time.perf_counter()
+                total += time.perf_counter() - t0
             torch.cuda.synchronize()
-            return (t1 - t0) * 1e3 / n
+            return total * 1e3 / n
 
         eager_ms = time_steps(opt_h.step, 20, 3, 1)
         eager_host = host_ms(opt_h.step)

@@ -116,6 +116,41 @@ def test_muon_apply_many_entries():
         assert_bits_equal(bits_of(p), ew.muon_apply(pb, ub, 0.02, 0.01, 1.7, 1000 + i), f"entry {i}")
 
 
+def test_launch_packing_with_empty_entries():
+    """More than one launch's worth of entries with empty tensors among them: every non-empty
+    entry is updated exactly once (the packer resumes where the previous launch stopped)."""
+    rng = np.random.default_rng(31)
+    sizes = [0, 0, 5] + [3, 0, 7] * 30  # 93 entries, 32 of them empty
+    ps = [rne_bf16((rng.standard_normal(n) * 0.02).astype(np.float32)) for n in sizes]
+    us = [rne_bf16((rng.standard_normal(n) * 0.1).astype(np.float32)) for n in sizes]
+    pg = [gpu(p) for p in ps]
+    K.muon_apply([(p, gpu(u), 1.3, 500 + i) for i, (p, u) in enumerate(zip(pg, us))], 0.02, 0.01)
+    for i, (p, pb, ub) in enumerate(zip(pg, ps, us)):
+        assert_bits_equal(bits_of(p), ew.muon_apply(pb, ub, 0.02, 0.01, 1.3, 500 + i), f"apply entry {i}")
+    gs = [rne_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)) for n in sizes]
+    pg, mg, vg = [gpu(p) for p in ps], [gpu(np.zeros(n, np.uint16)) for n in sizes], \
+        [gpu(np.zeros(n, np.uint16)) for n in sizes]
+    K.adamw_sr([(p, gpu(g), m, v, 2, 900 + i) for i, (p, g, m, v) in enumerate(zip(pg, gs, mg, vg))],
+               3e-4, 0.9, 0.95, 1e-10, 0.01)
+    for i, (p, pb, g) in enumerate(zip(pg, ps, gs)):
+        z = np.zeros(len(pb), np.uint16)
+        want = ew.adamw_sr(pb, g, z, z, 3e-4, 0.9, 0.95, 1e-10, 0.01, 2, 900 + i)[0]
+        assert_bits_equal(bits_of(p), want, f"adamw entry {i}")
+    n8 = [0] + [300] * 70  # 8-bit launcher: 64 entries per launch
+    q1, q2 = torch.from_numpy(o8.create_dynamic_map(True)).to(DEV), torch.from_numpy(o8.create_dynamic_map(False)).to(DEV)
+    p8 = [rne_bf16((rng.standard_normal(n) * 0.02).astype(np.float32)) for n in n8]
+    g8 = [rne_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)) for n in n8]
+    tp = [gpu(p) for p in p8]
+    st = [(gpu(np.zeros(n, np.uint16)), gpu(np.zeros(n, np.uint16))) for n in n8]
+    K.adamw8bit([(p, gpu(g), s1, s2, None, None, 1, 40 + i, False) for i, (p, g, (s1, s2)) in
+                 enumerate(zip(tp, g8, st))], q1, q2, 1e-3, 0.9, 0.999, 1e-8, 0.01, 256)
+    for i, (p, pb, g) in enumerate(zip(tp, p8, g8)):
+        z = np.zeros(len(pb), np.uint16)
+        want = o8.adamw8bit(pb, g, z, z, None, None, None, None, 1e-3, 0.9, 0.999, 1e-8, 0.01, 1, 40 + i, 256,
+                            False)[0]
+        assert_bits_equal(bits_of(p), want, f"8-bit entry {i}")
+
+
 def test_adamw_golden():
     d = load("adamw.npz")
     for k, (step, idx) in enumerate(zip(d["steps"].tolist(), d["idx"].tolist())):
