@@ -59,7 +59,7 @@ class _Launch:
 
 
 class _Recorder:
-    """Installed as ``kernels._recorder`` during a pass: "measure" sizes the records,
+    """Installed with ``kernels.recorder`` during a pass: "measure" sizes the records,
     "record" writes them and issues the replayable launches (inside the capture), "refresh"
     rewrites the scalars of a capture's records and issues nothing."""
 
@@ -188,13 +188,11 @@ class StepGraph:
             s.graph = torch.cuda.CUDAGraph()
             rec = _Recorder("record", s.host, s.dev)
             snap = _snapshot(optimizer)
-            K._recorder = rec
             try:
-                with torch.cuda.graph(s.graph, pool=pool):
+                with K.recorder(rec), torch.cuda.graph(s.graph, pool=pool):
                     s.dev.copy_(s.host, non_blocking=True)
                     optimizer.step()
             finally:
-                K._recorder = None
                 _restore(optimizer, snap)
             if [x.numels for x in rec.plan] != [x.numels for x in sizing.plan] or rec.constants != sizing.constants:
                 raise RuntimeError(_CHANGED)
@@ -210,11 +208,10 @@ class StepGraph:
 
     def _pass(self, rec):
         snap = _snapshot(self.optimizer)
-        K._recorder = rec
         try:
-            self.optimizer.step()
+            with K.recorder(rec):
+                self.optimizer.step()
         finally:
-            K._recorder = None
             _restore(self.optimizer, snap)
         return rec
 
@@ -226,13 +223,12 @@ class StepGraph:
         s.done.synchronize()  # the previous replay of this graph has read its records
         rec = _Recorder("refresh", s.host, s.dev, plan=s.plan, constants=s.constants)
         snap = _snapshot(self.optimizer)
-        K._recorder = rec
         ok = False
         try:
-            self.optimizer.step()
+            with K.recorder(rec):
+                self.optimizer.step()
             ok = rec.complete()
         finally:
-            K._recorder = None
             if not ok:
                 _restore(self.optimizer, snap)  # a refused step leaves the optimizer as it was
         if not ok:

@@ -5,8 +5,10 @@ Scalars that the reference evaluates from Python floats (``1 - beta``, ``1 - lr 
 ``lr / bias_correction`` ...) are computed here in double and rounded to fp32 once, as the
 reference's kernels see them.
 """
+import contextlib
 import ctypes
 import math
+import threading
 
 import numpy as np
 import torch
@@ -34,15 +36,29 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-# Set by ``graph.StepGraph`` while it sizes, captures or refreshes a step: the multi-tensor
-# launches below then go through it (replayable launches whose scalars live in a device
-# record), and in its passes that issue no kernels (``recorder.launches`` False) the
-# Newton-Schulz and centralisation calls return without launching.
-_recorder = None
+# ``recorder(rec)`` is entered by ``graph.StepGraph`` while it sizes, captures or refreshes a
+# step on this thread: the multi-tensor launches below then go through ``rec`` (replayable
+# launches whose scalars live in a device record), and in its passes that issue no kernels
+# (``rec.launches`` False) the Newton-Schulz and centralisation calls return without launching.
+_tls = threading.local()
+
+
+@contextlib.contextmanager
+def recorder(rec):
+    _tls.rec = rec
+    try:
+        yield rec
+    finally:
+        _tls.rec = None
+
+
+def _recorder():
+    return getattr(_tls, "rec", None)
 
 
 def _issuing():
-    return _recorder is None or _recorder.launches
+    rec = _recorder()
+    return rec is None or rec.launches
 
 
 # ---------------------------------------------------------------------------------------
@@ -79,9 +95,10 @@ def muon_prepare(items, beta: float, nesterov: bool) -> None:
         e.ctr_base = ctr_base & 0xFFFFFFFFFFFFFFFF
         e.key = triton_key(seed)
     dev = items[0][0].device
-    if _recorder is not None:
+    rec = _recorder()
+    if rec is not None:
         hdr = _lib.PrepareRecord(float(f32(beta)), float(f32(1.0 - beta)), int(bool(nesterov)), len(items))
-        _recorder.launch("msr_muon_prepare_rec", hdr, arr, dev)
+        rec.launch("msr_muon_prepare_rec", hdr, arr, dev)
         return
     _lib.check(_lib.load().msr_muon_prepare(arr, len(items), float(f32(beta)), float(f32(1.0 - beta)),
                                             int(bool(nesterov)), stream_handle(dev)), "msr_muon_prepare")
@@ -100,9 +117,10 @@ def muon_apply(items, lr: float, weight_decay: float) -> None:
         e.key = triton_key(seed)
         e.scale = float(f32(scale))
     dev = items[0][0].device
-    if _recorder is not None:
+    rec = _recorder()
+    if rec is not None:
         hdr = _lib.ApplyRecord(float(f32(lr)), float(f32(1.0 - lr * weight_decay)), len(items), 0)
-        _recorder.launch("msr_muon_apply_rec", hdr, arr, dev)
+        rec.launch("msr_muon_apply_rec", hdr, arr, dev)
         return
     _lib.check(_lib.load().msr_muon_apply(arr, len(items), float(f32(lr)), float(f32(1.0 - lr * weight_decay)),
                                           stream_handle(dev)), "msr_muon_apply")
@@ -125,8 +143,9 @@ def adamw_sr(items, lr: float, beta1: float, beta2: float, eps: float, weight_de
     hp = _lib.AdamWHparams(float(f32(beta1)), float(f32(1.0 - beta1)), float(f32(beta2)), float(f32(1.0 - beta2)),
                            float(f32(eps)), float(f32(1.0 - lr * weight_decay)))
     dev = items[0][0].device
-    if _recorder is not None:
-        _recorder.launch("msr_adamw_sr_rec", _lib.AdamWRecord(hp, len(items), 0), arr, dev)
+    rec = _recorder()
+    if rec is not None:
+        rec.launch("msr_adamw_sr_rec", _lib.AdamWRecord(hp, len(items), 0), arr, dev)
         return
     _lib.check(_lib.load().msr_adamw_sr(arr, len(items), ctypes.byref(hp), stream_handle(dev)), "msr_adamw_sr")
 
@@ -150,7 +169,7 @@ def quant_tables(qmap1: torch.Tensor, qmap2: torch.Tensor):
 def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_size, qtables=None) -> None:
     """items: iterable of (param, grad, state1, state2, absmax1, absmax2, step, seed, quantized).
     ``qtables``: the lookup-table blob of ``quant_tables`` (None runs the codebook walk)."""
-    if _recorder is not None:
+    if _recorder() is not None:
         raise RuntimeError("8-bit AdamW launches cannot be captured in a StepGraph")
     items = list(items)
     if not items:
@@ -254,9 +273,10 @@ def centralize(grad: torch.Tensor, centralization: float) -> torch.Tensor:
     """``bf16(g - c * g.mean(dim=trailing dims, keepdim=True))`` with the mean in fp32, as
     TritonAdamW's centralization (muon_sr/triton_adamw.py:179-187), in one fused kernel;
     returns a new bf16 tensor."""
-    if _recorder is not None:
-        _recorder.constant("centralization", float(centralization))
-        if not _recorder.launches:
+    rec = _recorder()
+    if rec is not None:
+        rec.constant("centralization", float(centralization))
+        if not rec.launches:
             return grad
     g = grad if grad.is_contiguous() else grad.contiguous()
     _require(g, "grad")
