@@ -7,12 +7,14 @@
 // moves 8 bf16 per 16-byte access, issuing all loads of a chunk before its math so that
 // every SM keeps enough bytes in flight for HBM3e. All fp32 arithmetic uses explicit
 // round-to-nearest intrinsics (no contraction into FMA), in the reference's op order, so
-// results are bit-identical to the reference kernels' fp32 evaluation.
+// results are bit-identical to the reference kernels' fp32 evaluation. Every kernel is
+// instantiated per noise mode (msr_set_sr_noise), and prepare / apply / AdamW once more
+// (REC) for the replayable launches that read their scalars and entries from a device
+// record (msr_*_rec, used inside captured CUDA graphs).
 #include "common.cuh"
 #include "host_common.h"
 
 #include <algorithm>
-#include <vector>
 
 namespace msr {
 namespace {

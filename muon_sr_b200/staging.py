@@ -34,11 +34,6 @@ _tls = threading.local()
 BATCH_NUMEL = 1 << 28
 
 
-def active():
-    """The HostStaging of the step being issued on this thread, or None."""
-    return getattr(_tls, "io", None)
-
-
 def need(params):
     """Announce that the next launch reads the gradients of ``params``."""
     io = getattr(_tls, "io", None)
