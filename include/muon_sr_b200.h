@@ -52,6 +52,9 @@ int msr_abi_version(void);
  * Returns MSR_ERR_INVALID for an unknown mode. */
 enum msr_sr_noise { MSR_SR_NOISE_REFERENCE = 0, MSR_SR_NOISE_FAST = 1, MSR_SR_NOISE_NONE = 2 };
 int msr_set_sr_noise(int mode);
+/* The current mode (MSR_SR_NOISE_*). The Python layer applies the environment variable
+ * MSR_SR_NOISE=reference|fast|none when it loads the library. */
+int msr_get_sr_noise(void);
 /* Static description of a status code. */
 const char* msr_status_string(int status);
 /* Detail message of the last failing call on the calling host thread ("" if none). */
@@ -78,6 +81,8 @@ void msr_set_gemm_max_ctas(int max_ctas);
  * 128 x 256 tiles on single SMs. Both give the same results; process-wide. No counterpart
  * in the reference (its GEMMs are cuBLAS calls). */
 void msr_set_gemm_pairs(int enable);
+/* 1 if SM-pair tiles are selected (the default); the Python layer applies MSR_GEMM_PAIRS=0|1. */
+int msr_get_gemm_pairs(void);
 
 /* ---- Philox (test hook) ------------------------------------------------------------
  * out[i] = word 0 of Philox4x32-10 with counter ((ctr_base + i) mod 2^32, 0, 0, 0) and key

@@ -69,6 +69,7 @@ class Adam8Hparams(ctypes.Structure):
 SIGNATURES = [
     ("msr_abi_version", c_int, []),
     ("msr_set_sr_noise", c_int, [c_int]),
+    ("msr_get_sr_noise", c_int, []),
     ("msr_status_string", ctypes.c_char_p, [c_int]),
     ("msr_last_error", ctypes.c_char_p, []),
     ("msr_device_error", c_int, [c_void_p, c_int]),
@@ -76,6 +77,7 @@ SIGNATURES = [
     ("msr_launch_count", c_uint64, []),
     ("msr_set_gemm_max_ctas", None, [c_int]),
     ("msr_set_gemm_pairs", None, [c_int]),
+    ("msr_get_gemm_pairs", c_int, []),
     ("msr_philox_fill", c_int, [c_void_p, c_int64, c_uint64, c_uint64, c_void_p]),
     ("msr_grad_accum_bf16", c_int, [c_void_p, c_void_p, c_int64, c_uint64, c_int, c_void_p]),
     ("msr_muon_prepare", c_int, [ctypes.POINTER(PrepareEntry), c_int, c_float, c_float, c_int, c_void_p]),
@@ -125,8 +127,28 @@ def load():
                 fn = getattr(lib, name)
                 fn.restype = restype
                 fn.argtypes = argtypes
+            _apply_env(lib)
             _lib = lib
     return _lib
+
+
+# Process-wide debug knobs read once, when the library loads: MSR_SR_NOISE selects the
+# stochastic-rounding noise ("none" = round to nearest, the parity mode), MSR_GEMM_PAIRS=0
+# the single-SM GEMM tiles. Both give the same API; see msr_set_sr_noise / msr_set_gemm_pairs.
+ENV_SR_NOISE = {"reference": 0, "fast": 1, "none": 2}
+
+
+def _apply_env(lib):
+    noise = os.environ.get("MSR_SR_NOISE")
+    if noise:
+        if noise not in ENV_SR_NOISE:
+            raise ValueError(f"MSR_SR_NOISE must be one of {sorted(ENV_SR_NOISE)}, got {noise!r}")
+        lib.msr_set_sr_noise(ENV_SR_NOISE[noise])
+    pairs = os.environ.get("MSR_GEMM_PAIRS")
+    if pairs:
+        if pairs not in ("0", "1"):
+            raise ValueError(f"MSR_GEMM_PAIRS must be 0 or 1, got {pairs!r}")
+        lib.msr_set_gemm_pairs(int(pairs))
 
 
 def check(status: int, what: str) -> None:

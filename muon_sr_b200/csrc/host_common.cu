@@ -63,6 +63,8 @@ int msr_set_sr_noise(int mode) {
   return MSR_OK;
 }
 
+int msr_get_sr_noise(void) { return msr::sr_noise_mode(); }
+
 const char* msr_status_string(int status) {
   switch (status) {
     case MSR_OK: return "ok";

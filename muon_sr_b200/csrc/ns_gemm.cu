@@ -996,6 +996,8 @@ void msr_set_gemm_max_ctas(int max_ctas) { g_gemm_max_ctas.store(max_ctas > 0 ? 
 
 void msr_set_gemm_pairs(int enable) { g_gemm_pairs.store(enable ? 1 : 0); }
 
+int msr_get_gemm_pairs(void) { return g_gemm_pairs.load(); }
+
 int msr_test_wait_timeout(uint64_t limit_ns, msr_stream_t stream) {
   if (limit_ns == 0 || limit_ns > 10000000000ull)
     return fail(MSR_ERR_INVALID, "msr_test_wait_timeout: limit must be in (0, 10 s]");

@@ -78,3 +78,22 @@ def test_more_argument_errors_without_gpu():
     # zero-length and empty requests are no-ops
     assert lib.msr_copy_async(None, None, 0, None) == 0
     assert lib.msr_muon_prepare(None, 0, 0.9, 0.1, 1, None) == 0
+
+
+def test_env_knobs_apply_at_load():
+    """MSR_SR_NOISE and MSR_GEMM_PAIRS are applied once, when the library loads; a bad value
+    is refused with a message naming the variable."""
+    import subprocess
+    import sys
+    code = ("from muon_sr_b200 import _lib; l = _lib.load(); "
+            "print(l.msr_get_sr_noise(), l.msr_get_gemm_pairs())")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+    def run(env):
+        return subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
+                              env=dict(os.environ, **env), timeout=300)
+    assert run({}).stdout.split() == ["0", "1"]
+    assert run({"MSR_SR_NOISE": "none", "MSR_GEMM_PAIRS": "0"}).stdout.split() == ["2", "0"]
+    assert run({"MSR_SR_NOISE": "fast"}).stdout.split() == ["1", "1"]
+    bad = run({"MSR_SR_NOISE": "xoshiro"})
+    assert bad.returncode != 0 and "MSR_SR_NOISE" in bad.stderr
