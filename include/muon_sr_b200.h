@@ -322,6 +322,14 @@ int msr_gemm_bf16(const void* a, int a_mn_major, const void* b, int b_mn_major, 
                   void* d, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha, float beta,
                   const float* scale, int alpha_pow, int beta_pow, int flags, msr_stream_t stream);
 
+/* Test hook, host only (no GPU needed): the GEMM kernels' tile schedule. Sets *num_tiles to
+ * the number of output tiles a launch of this shape runs (`pairs`: 256 x 256 SM-pair tiles,
+ * else 128 x 256; `symmetric`: only tiles touching the upper triangle, M == N) and, if `out`
+ * holds 3 * num_tiles values, writes (matrix, first row, first column) of each linear tile
+ * index in the order the persistent kernels take them -- the same decoding the kernels run. */
+int msr_gemm_tile_map(int64_t M, int64_t N, int64_t batch, int symmetric, int pairs, int64_t* out,
+                      int64_t capacity, int64_t* num_tiles);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,6 +105,8 @@ SIGNATURES = [
     ("msr_event_destroy", c_int, [c_void_p]),
     ("msr_gemm_bf16", c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                               c_int64, c_float, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
+    ("msr_gemm_tile_map", c_int, [c_int64, c_int64, c_int64, c_int, c_int, ctypes.POINTER(c_int64), c_int64,
+                                  ctypes.POINTER(c_int64)]),
 ]
 
 _lib = None

@@ -84,7 +84,7 @@ constexpr int64_t GROUP_M = 8;
 // an element on or above the diagonal). In a band starting at row-block g0 (a multiple of
 // RHO), column k = g0 / RHO + d holds the band's first min(R, RHO (d + 1)) row-blocks.
 template <int RHO>
-__device__ __forceinline__ int64_t sym_band_tiles(int64_t R, int64_t D) {
+__host__ __device__ __forceinline__ int64_t sym_band_tiles(int64_t R, int64_t D) {
   // sum_{d < D} min(R, RHO (d + 1)): a ramp of dr columns, then full columns of R
   const int64_t ramp = R / RHO;
   const int64_t dr = D < ramp ? D : ramp;
@@ -93,16 +93,20 @@ __device__ __forceinline__ int64_t sym_band_tiles(int64_t R, int64_t D) {
   return s;
 }
 
-// Linear tile index -> (matrix, first row, first column).
+__host__ __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// Linear tile index -> (matrix, first row, first column). Host-callable, so that the tile
+// map can be checked without a GPU (msr_gemm_tile_map).
 template <int TILE_M>
-__device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t& b, int64_t& m0, int64_t& n0) {
+__host__ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t& b, int64_t& m0,
+                                                     int64_t& n0) {
   constexpr int RHO = BN / TILE_M;
   b = t / p.tiles_per_batch;
   int64_t r = t % p.tiles_per_batch;
   if (!p.sym) {
     const int64_t band_tiles = GROUP_M * p.tiles_n;
     const int64_t g0 = (r / band_tiles) * GROUP_M;
-    const int64_t R = min(GROUP_M, p.tiles_m - g0);
+    const int64_t R = imin(GROUP_M, p.tiles_m - g0);
     const int64_t w = r % band_tiles;
     m0 = (g0 + w % R) * TILE_M;
     n0 = (w / R) * BN;
@@ -110,17 +114,17 @@ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t, int64_t&
   }
   int64_t g0 = 0;
   for (;;) {
-    const int64_t R = min(GROUP_M, p.tiles_m - g0);
+    const int64_t R = imin(GROUP_M, p.tiles_m - g0);
     const int64_t cnt = sym_band_tiles<RHO>(R, p.tiles_n - g0 / RHO);
     if (r < cnt) break;
     r -= cnt;
     g0 += GROUP_M;
   }
-  const int64_t R = min(GROUP_M, p.tiles_m - g0);
+  const int64_t R = imin(GROUP_M, p.tiles_m - g0);
   // column offset d: the ramp columns hold RHO (d + 1) rows each, later ones R
   int64_t d = 0, rows_d = 0;
   for (;;) {
-    rows_d = min(R, RHO * (d + 1));
+    rows_d = imin(R, RHO * (d + 1));
     if (r < rows_d) break;
     r -= rows_d;
     ++d;
@@ -793,6 +797,22 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, c
   return check_launch("gemm_pair_kernel");
 }
 
+// The tile grid of a GEMM: tiles of tile_m x BN over [M][N] per matrix; in symmetric mode
+// row-block i keeps column-blocks i / RHO .. tiles_n - 1 (see decode_tile).
+void set_tiles(Params& p, int64_t M, int64_t N, int64_t batch, int sym, int64_t tile_m) {
+  p.M = M; p.N = N; p.batch = batch;
+  p.tiles_m = (M + tile_m - 1) / tile_m;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.sym = sym;
+  p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  if (sym) {
+    const int64_t rho = BN / tile_m;
+    p.tiles_per_batch = 0;
+    for (int64_t i = 0; i < p.tiles_m; ++i) p.tiles_per_batch += p.tiles_n - i / rho;
+  }
+  p.num_tiles = p.tiles_per_batch * batch;
+}
+
 // D[b] = alpha_b * op(A)[b] x op(B)[b]^T + beta_b * C[b]. A K-major: [batch][M][K]; MN-major:
 // [batch][K][M]. B K-major: [batch][N][K]; MN-major: [batch][K][N]. C, D: [batch][M][N] with
 // row strides ldc, ldd.
@@ -811,18 +831,8 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
   st = b_mn ? make_map(&tb, b, N, K, batch, b_bstride, 64) : make_map(&tb, b, K, N, batch, b_bstride, b_rows);
   if (st) return st;
   Params p{};
-  p.M = M; p.N = N; p.K = K; p.batch = batch;
-  p.tiles_m = (M + tile_m - 1) / tile_m;
-  p.tiles_n = (N + BN - 1) / BN;
-  p.sym = sym;
-  p.tiles_per_batch = p.tiles_m * p.tiles_n;
-  if (sym) {
-    // row-block i keeps column-blocks i / RHO .. tiles_n - 1 (see decode_tile)
-    const int64_t rho = BN / tile_m;
-    p.tiles_per_batch = 0;
-    for (int64_t i = 0; i < p.tiles_m; ++i) p.tiles_per_batch += p.tiles_n - i / rho;
-  }
-  p.num_tiles = p.tiles_per_batch * batch;
+  p.K = K;
+  set_tiles(p, M, N, batch, sym, tile_m);
   p.d = static_cast<uint16_t*>(d);
   p.c = static_cast<const uint16_t*>(c);
   p.ldd = ldd; p.ldc = ldc; p.d_bstride = d_bstride; p.c_bstride = c_bstride;
@@ -995,6 +1005,27 @@ extern "C" {
 void msr_set_gemm_max_ctas(int max_ctas) { g_gemm_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
 
 void msr_set_gemm_pairs(int enable) { g_gemm_pairs.store(enable ? 1 : 0); }
+
+int msr_gemm_tile_map(int64_t M, int64_t N, int64_t batch, int symmetric, int pairs, int64_t* out, int64_t capacity,
+                      int64_t* num_tiles) {
+  if (M <= 0 || N <= 0 || batch <= 0 || !num_tiles || (symmetric && M != N))
+    return fail(MSR_ERR_INVALID, "msr_gemm_tile_map: bad shape");
+  Params p{};
+  set_tiles(p, M, N, batch, symmetric ? 1 : 0, pairs ? pair::TILE_M : BM);
+  *num_tiles = p.num_tiles;
+  if (out == nullptr) return MSR_OK;
+  if (capacity < 3 * p.num_tiles) return fail(MSR_ERR_INVALID, "msr_gemm_tile_map: out holds fewer than 3 x %lld",
+                                              (long long)p.num_tiles);
+  for (int64_t t = 0; t < p.num_tiles; ++t) {
+    int64_t b, m0, n0;
+    if (pairs) decode_tile<pair::TILE_M>(p, t, b, m0, n0);
+    else decode_tile<BM>(p, t, b, m0, n0);
+    out[3 * t] = b;
+    out[3 * t + 1] = m0;
+    out[3 * t + 2] = n0;
+  }
+  return MSR_OK;
+}
 
 int msr_get_gemm_pairs(void) { return g_gemm_pairs.load(); }
 

@@ -4,6 +4,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 
 from muon_sr_b200 import _lib
 
@@ -97,3 +99,47 @@ def test_env_knobs_apply_at_load():
     assert run({"MSR_SR_NOISE": "fast"}).stdout.split() == ["1", "1"]
     bad = run({"MSR_SR_NOISE": "xoshiro"})
     assert bad.returncode != 0 and "MSR_SR_NOISE" in bad.stderr
+
+
+def _tile_map(M, N, batch, sym, pairs):
+    lib = _lib.load()
+    n = ctypes.c_int64()
+    assert lib.msr_gemm_tile_map(M, N, batch, sym, pairs, None, 0, ctypes.byref(n)) == 0
+    out = (ctypes.c_int64 * (3 * n.value))()
+    assert lib.msr_gemm_tile_map(M, N, batch, sym, pairs, out, 3 * n.value, ctypes.byref(n)) == 0
+    return [tuple(out[3 * i:3 * i + 3]) for i in range(n.value)]
+
+
+@pytest.mark.parametrize("pairs", [0, 1])
+def test_gemm_tile_schedule_covers_each_tile_once(pairs):
+    """The persistent GEMM's tile decoding, run on the host: every output tile of every matrix
+    exactly once (full GEMMs), and in symmetric mode exactly the tiles that hold an element
+    on or above the diagonal -- whose mirror-writes then cover the rest."""
+    tm, bn = (256 if pairs else 128), 256
+    sizes = [1, 100, 128, 129, 255, 256, 257, 768, 1000, 1024, 2049, 4096]
+    for M in sizes:
+        for N in sizes[::3] + [M]:
+            for batch in (1, 3):
+                got = _tile_map(M, N, batch, 0, pairs)
+                want = [(b, i * tm, k * bn) for b in range(batch) for i in range(-(-M // tm))
+                        for k in range(-(-N // bn))]
+                assert sorted(got) == sorted(want) and len(got) == len(want), (M, N, batch)
+        for batch in (1, 2):
+            got = _tile_map(M, M, batch, 1, pairs)
+            want = [(b, i * tm, k * bn) for b in range(batch) for i in range(-(-M // tm))
+                    for k in range(-(-M // bn)) if k * bn + bn > i * tm]  # tile reaches the diagonal
+            assert sorted(got) == sorted(want) and len(got) == len(set(got)), (M, batch)
+    # grouped rasterisation: consecutive tiles stay within bands of 8 row-blocks
+    got = _tile_map(4096, 14336, 1, 0, pairs)
+    band = [m // (8 * tm) for _, m, _ in got]
+    assert band == sorted(band)
+
+
+def test_gemm_tile_map_argument_errors():
+    lib = _lib.load()
+    n = ctypes.c_int64()
+    assert lib.msr_gemm_tile_map(0, 8, 1, 0, 0, None, 0, ctypes.byref(n)) == 1
+    assert lib.msr_gemm_tile_map(8, 16, 1, 1, 0, None, 0, ctypes.byref(n)) == 1  # symmetric needs M == N
+    assert lib.msr_gemm_tile_map(300, 300, 1, 0, 0, None, 0, ctypes.byref(n)) == 0
+    out = (ctypes.c_int64 * 3)()
+    assert lib.msr_gemm_tile_map(300, 300, 1, 0, 0, out, 3, ctypes.byref(n)) == 1  # too small
