@@ -47,6 +47,21 @@ def _side_streams(device):
     return entry
 
 
+# In a stack of several Newton-Schulz chunks run on the step's stream (not sharded), the
+# prepare of chunk c + 1 and the apply of chunk c run on a second stream while chunk c's
+# Newton-Schulz runs, so the elementwise kernels use the SMs the GEMMs' last waves leave
+# idle. Same kernels and counters: the same bits.
+PIPELINE_CHUNKS = True
+_ew = {}
+
+
+def _ew_stream(device):
+    s = _ew.get(device.index)
+    if s is None:
+        s = _ew[device.index] = torch.cuda.Stream(device)
+    return s
+
+
 # ---------------------------------------------------------------------------------------
 # Step state
 # ---------------------------------------------------------------------------------------
@@ -195,7 +210,7 @@ def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, se
             side.wait_event(start)
             with torch.cuda.stream(side):
                 _stack_step(s, shape, members, stacks.tensor[shape], beta, nesterov, ns_steps, lr, weight_decay,
-                            step, seeder, work)
+                            step, seeder, work, pipeline=False)
             used.append(side)
         else:
             _stack_step(s, shape, members, stacks.tensor[shape], beta, nesterov, ns_steps, lr, weight_decay, step,
@@ -206,7 +221,8 @@ def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, se
         main.wait_stream(side)
 
 
-def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work):
+def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work,
+                pipeline=True):
     """One shape stack of ``muon_batch_step``. With ``work.segments`` the stack's rows are cut
     into consecutive segments; each rank runs its own rows segment by segment and
     ``work.share`` is called after every segment (on every rank, also when it owned none of
@@ -236,6 +252,10 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
     apply_seed = [seeder(step, s * 10000 + r, 1) for r in range(len(members))]
     chunk = max(1, NS_CHUNK_NUMEL // max(1, numel))
     scale = K.ns_scale(shape)
+    if pipeline and PIPELINE_CHUNKS and work.share is None and momentum.is_cuda and len(rows) > chunk:
+        _pipelined_chunks(members, rows, chunk, momentum, numel, prep_seed, apply_seed, scale, shape, beta, nesterov,
+                          ns_steps, lr, weight_decay)
+        return
     upd = torch.empty((min(chunk, len(rows)),) + tuple(shape), dtype=torch.bfloat16, device=momentum.device) \
         if rows else None
     lo = 0  # first position in `rows` of the current segment
@@ -259,6 +279,57 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
         if len(parts) > 1:
             work.share([members[r] for r in part])
     del upd
+
+
+def _pipelined_chunks(members, rows, chunk, momentum, numel, prep_seed, apply_seed, scale, shape, beta, nesterov,
+                      ns_steps, lr, weight_decay):
+    """The chunk loop of ``_stack_step`` with the elementwise work on a second stream: prepare
+    of chunk i + 1 and apply of chunk i overlap the Newton-Schulz of chunk i. Two update
+    buffers alternate; the prepare writing one waits until the Newton-Schulz two chunks back
+    has read it. The current stream waits for the second one at the end."""
+    device = momentum.device
+    main = torch.cuda.current_stream(device)
+    ew = _ew_stream(device)
+    groups = [rows[c:c + chunk] for c in range(0, len(rows), chunk)]
+    bufs = [torch.empty((chunk,) + tuple(shape), dtype=torch.bfloat16, device=device) for _ in range(2)]
+    start = torch.cuda.Event()
+    start.record(main)
+    ew.wait_event(start)
+    ns_done = []
+
+    def prepare(i):
+        with torch.cuda.stream(ew):
+            if i >= 2:
+                ew.wait_event(ns_done[i - 2])
+            mine = [members[r] for r in groups[i]]
+            staging.need(mine)
+            x = bufs[i % 2][:len(mine)]
+            K.muon_prepare([(_grad_of(p), momentum[r], x[j], r * numel, prep_seed)
+                            for j, (p, r) in enumerate(zip(mine, groups[i]))], beta, nesterov)
+            ready = torch.cuda.Event()
+            ready.record(ew)
+        return x, ready
+
+    nxt = prepare(0)
+    for i, grp in enumerate(groups):
+        x, ready = nxt
+        main.wait_event(ready)
+        out = K.newton_schulz(x, ns_steps)
+        done = torch.cuda.Event()
+        done.record(main)
+        ns_done.append(done)
+        if i + 1 < len(groups):
+            nxt = prepare(i + 1)
+        with torch.cuda.stream(ew):
+            ew.wait_event(done)
+            out.record_stream(ew)
+            mine = [members[r] for r in grp]
+            K.muon_apply([(p, out[j], scale, apply_seed[r]) for j, (p, r) in enumerate(zip(mine, grp))], lr,
+                         weight_decay)
+            staging.done(mine)
+        del out
+    main.wait_stream(ew)
+    del bufs
 
 
 # ---------------------------------------------------------------------------------------
