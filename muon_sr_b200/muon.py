@@ -47,11 +47,12 @@ def _side_streams(device):
     return entry
 
 
-# In a stack of several Newton-Schulz chunks run on the step's stream (not sharded), the
-# prepare of chunk c + 1 and the apply of chunk c run on a second stream while chunk c's
-# Newton-Schulz runs, so the elementwise kernels use the SMs the GEMMs' last waves leave
-# idle. Same kernels and counters: the same bits.
-PIPELINE_CHUNKS = True
+# Option: in a stack of several Newton-Schulz chunks run on the step's stream (not sharded),
+# the prepare of chunk c + 1 and the apply of chunk c run on a second stream while chunk c's
+# Newton-Schulz runs. Same kernels and counters: the same bits. Off by default: measured on
+# B200 in the Llama-3-8B step, 461.8 / 461.9 ms with it vs 461.8 / 463.3 ms without -- the
+# step is bound by the 1 kW power cap, so overlapping moves energy around without saving it.
+PIPELINE_CHUNKS = False
 _ew = {}
 
 
