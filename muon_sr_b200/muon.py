@@ -228,7 +228,9 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
     into consecutive segments; each rank runs its own rows segment by segment and
     ``work.share`` is called after every segment (on every rank, also when it owned none of
     it), so the weights start travelling while the rest of the stack computes. Chunks never
-    span segments; the bits are those of the unsegmented step."""
+    span segments; the bits are those of the unsegmented step. ``pipeline`` allows the
+    pipelined chunk loop (``PIPELINE_CHUNKS``); stacks that already run on a side stream
+    pass False."""
     if all(p.grad is None for p in members):
         return
     if any(p.grad is None for p in members):
