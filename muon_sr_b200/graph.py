@@ -176,6 +176,7 @@ class StepGraph:
             raise RuntimeError("run one eager optimizer.step() before capturing it")
         self._device = with_grad[0].device
         self._grads = self._grad_ptrs()
+        self._storage = self._storage_ptrs()
 
         sizing = self._pass(_Recorder("measure"))
         size = max(16, sizing.size)
@@ -206,6 +207,16 @@ class StepGraph:
     def _grad_ptrs(self):
         return [p.grad.data_ptr() if p.grad is not None else None for p in self._params]
 
+    def _storage_ptrs(self):
+        """Where the parameters and their state tensors live: the captured kernels write there,
+        so a replay after any of them moved (``load_state_dict`` rebuilds the momentum stacks,
+        ``.to()`` moves parameters) would write to stale memory and is refused."""
+        out = []
+        for p in self._params:
+            st = self.optimizer.state.get(p, {})
+            out.append((p.data_ptr(), tuple((k, v.data_ptr()) for k, v in sorted(st.items()) if torch.is_tensor(v))))
+        return out
+
     def _pass(self, rec):
         snap = _snapshot(self.optimizer)
         try:
@@ -217,7 +228,7 @@ class StepGraph:
 
     def step(self):
         """One optimizer step: refresh the scalars on the host, replay the graph."""
-        if self._grad_ptrs() != self._grads:
+        if self._grad_ptrs() != self._grads or self._storage_ptrs() != self._storage:
             raise RuntimeError(_CHANGED)
         s = self._slots[self._next]
         s.done.synchronize()  # the previous replay of this graph has read its records
@@ -227,7 +238,8 @@ class StepGraph:
         try:
             with K.recorder(rec):
                 self.optimizer.step()
-            ok = rec.complete()
+            # the pass itself may have moved state (momentum stacks rebuilt after a load)
+            ok = rec.complete() and self._storage_ptrs() == self._storage
         finally:
             if not ok:
                 _restore(self.optimizer, snap)  # a refused step leaves the optimizer as it was

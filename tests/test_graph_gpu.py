@@ -129,6 +129,10 @@ def test_graph_refuses_changed_structure(small_chunks):
     params[0].grad = torch.zeros_like(params[0])     # another tensor behind a .grad
     with pytest.raises(RuntimeError, match="captured graph"):
         graph.step()
+    graph, opt, params = _run(lambda ps: TritonMuonSR(ps, lr=0.02, weight_decay=0.01, batch_ns=True), MUON, steps=1)
+    opt.load_state_dict(opt.state_dict())            # new state tensors: the graph's pointers are stale
+    with pytest.raises(RuntimeError, match="captured graph"):
+        graph.step()
 
 
 def test_graph_argument_errors():
