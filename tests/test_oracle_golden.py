@@ -120,3 +120,21 @@ def test_fast_noise_stream_layout():
     assert vals.max() < 1 << 16
     hist = np.bincount(vals >> 12, minlength=16)  # 16 bins of a uniform 16-bit value
     assert hist.min() > 0.9 * (1 << 12) and hist.max() < 1.1 * (1 << 12)
+
+
+def test_round_to_nearest_mode_is_the_fp32_formula_cast():
+    """noise="none" (the engine's parity mode) is the reference formula in fp32 rounded to
+    nearest even -- the same fp32 values the SR modes round stochastically."""
+    from oracle.sr import bf16_to_f32
+    rng = np.random.default_rng(9)
+    n = 4096
+    a, g = rne_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)), \
+        rne_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32))
+    want = rne_bf16((bf16_to_f32(a) + bf16_to_f32(g)).astype(np.float32))
+    assert_bits_equal(ew.grad_accum(a, g, 5, noise="none"), want, "grad_accum rtn")
+    sr = ew.grad_accum(a, g, 5)
+    # SR lands on one of the two bf16 neighbours of the fp32 sum; RTN on the nearer one
+    s = (bf16_to_f32(a) + bf16_to_f32(g)).astype(np.float32)
+    lo = truncate_bf16(s)
+    assert np.all((sr == lo) | (sr == lo + 1) | (s == 0))
+    assert np.all((want == lo) | (want == lo + 1) | (s == 0))
