@@ -20,6 +20,7 @@ NVLink / NVSwitch, so the step's work is divided by the number of ranks.
   only has to reach its owner.
 """
 import ctypes
+import datetime
 import heapq
 import os
 import warnings
@@ -37,6 +38,7 @@ ADAMW_BYTES = 1.0e12       # 14 B per element, three Philox streams
 ADAMW8BIT_BYTES = 1.28e12  # 10.0625 B per element
 SEGMENT_SECONDS = 4e-3  # per-rank Newton-Schulz time between two weight shares of a stack
 COPY_STREAMS_PER_PEER = 2
+HOST_BARRIER_TIMEOUT = datetime.timedelta(seconds=300)
 
 
 def _ns_flops(shape, steps=5):
@@ -104,8 +106,10 @@ class Sharder:
             warnings.warn("Sharder(transport='p2p') runs several copy streams per peer next to the compute stream; "
                           "set CUDA_DEVICE_MAX_CONNECTIONS=32 before CUDA initialises, or copies waiting on peers "
                           "can delay compute kernels that share their hardware queue", RuntimeWarning)
-        # host-only barriers for the p2p ordering (created collectively, same order on all ranks)
-        self._host = dist.new_group(backend="gloo") if self.transport == "p2p" else None
+        # host-only barriers for the p2p ordering (created collectively, same order on all ranks);
+        # they only wait for the other ranks to issue their work, so a rank that failed ends
+        # the others' wait with an error after HOST_BARRIER_TIMEOUT instead of torch's default
+        self._host = dist.new_group(backend="gloo", timeout=HOST_BARRIER_TIMEOUT) if self.transport == "p2p" else None
         self._owner = None  # id(param) -> rank within the group
         self._order = None  # params in a fixed order
         self._p2p = None    # lazily built peer mappings
