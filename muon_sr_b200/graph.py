@@ -176,7 +176,7 @@ class StepGraph:
             raise RuntimeError("run one eager optimizer.step() before capturing it")
         self._device = with_grad[0].device
         self._grads = self._grad_ptrs()
-        self._storage = self._storage_ptrs()
+        self._storage = None  # where the captured kernels write: taken after the first capture
 
         sizing = self._pass(_Recorder("measure"))
         size = max(16, sizing.size)
@@ -197,6 +197,10 @@ class StepGraph:
                 _restore(optimizer, snap)
             if [x.numels for x in rec.plan] != [x.numels for x in sizing.plan] or rec.constants != sizing.constants:
                 raise RuntimeError(_CHANGED)
+            storage = self._storage_ptrs()  # a pass may have built state (stacks after a load)
+            if self._storage is not None and storage != self._storage:
+                raise RuntimeError(_CHANGED)
+            self._storage = storage
             pool = s.graph.pool()
             s.plan, s.constants = rec.plan, rec.constants
             s.done = torch.cuda.Event()
