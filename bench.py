@@ -371,13 +371,16 @@ def run_ours(args, rank, world, local_rank):
         eager_host = host_ms(opt_h.step)
         extra.update({"gpt2_hybrid_step_ms": eager_ms, "gpt2_hybrid_host_issue_ms": eager_host,
                       "gpt2_hybrid_ns_tflops": sum(ns_flops(p.shape) for p in mats) / (eager_ms * 1e-3) / 1e12})
-        try:
-            sg = StepGraph(opt_h)
-            extra.update({"gpt2_hybrid_step_ms_graph": time_steps(sg.step, 20, 3, 1),
-                          "gpt2_hybrid_host_issue_ms_graph": host_ms(sg.step)})
-            del sg
-        except RuntimeError as exc:  # reported, not fatal: the headline does not use graphs
-            extra["gpt2_hybrid_graph_error"] = str(exc)[:300]
+        # single-process runs only: a stream capture in global mode while an NCCL process group
+        # is alive could make the communicator's background threads' CUDA calls fail
+        if world == 1:
+            try:
+                sg = StepGraph(opt_h)
+                extra.update({"gpt2_hybrid_step_ms_graph": time_steps(sg.step, 20, 3, 1),
+                              "gpt2_hybrid_host_issue_ms_graph": host_ms(sg.step)})
+                del sg
+            except RuntimeError as exc:  # reported, not fatal: the headline does not use graphs
+                extra["gpt2_hybrid_graph_error"] = str(exc)[:300]
         del opt_h, mats
         del opt_a, gpt2
         torch.cuda.empty_cache()
