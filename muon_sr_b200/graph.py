@@ -21,7 +21,9 @@ StepGraph does not advance the optimizer.
 
 Requirements: one eager ``step()`` before construction (the optimizer state exists); the
 parameters, their ``.grad`` tensors and the optimizer state keep their storage; one stream;
-no ``Sharder``. The 8-bit optimizer is not captured (its step is one launch).
+no ``Sharder``. The 8-bit optimizer is not captured (its step is one launch). The capture
+uses CUDA's global capture mode, so no other thread of the process should issue CUDA work
+(e.g. collectives in flight) while a StepGraph is being built.
 
 The replay saves the host's launch work -- the per-launch C-ABI and CUDA launch costs, most
 of all the ~16 launches and tensor-map encodings of every Newton-Schulz call -- which matters
