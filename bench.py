@@ -13,8 +13,17 @@ The same run also times the 8-bit blockwise AdamW step on the same 
 same step through the public API with the step's gradients copied in from pinned host
 memory and the updated weights copied back out (``HostStaging``: copies overlapped with the
 step chunk by chunk; ``e2e_serial``: all uploads, then the step, then all downloads).
-``--impl reference`` times the reference's pure-PyTorch MuonSR / AdamW-SR step (restated in
-``oracle/``) on the host cores on a bounded sample and scales it to a full step.
+``--impl reference`` times the reference's own pure-PyTorch ``MuonSRWithAuxAdam`` step (the
+unmodified package installed in ``baseline/_ref``; the ``oracle/`` restatement only if that
+install is missing) on the host cores, on a bounded sample scaled to a full step
+(``extrapolated`` in the line says so).
+
+With one GPU the line also carries ``reference_gpu``: the reference's own Triton kernels and
+torch/cuBLAS Newton-Schulz (``baseline/_ref``) timed on the same GPU on the same synthetic
+inputs, beside this engine's numbers for the same work, and ``cpu_reference_configs0``: the
+reference's ``MuonSR.step()`` on the whole GPT-2-small matrix set on the host
+cores, not extrapolated. With several GPUs, ``sharded_bit_identical`` reports whether a small
+sharded hybrid step and 8-bit step wrote the same bits as the unsharded step on every rank.
 """
 import argparse
 import datetime
@@ -38,8 +47,9 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "Llama-3-8B hybrid optimizer step ms; NS TFLOP/s; 8-bit AdamW HBM GB/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one adamw8bit_kernel launch on 2^28 elements
-# (block 256), from the capture summarised in profiles/adamw8bit_kernel_256M.md
+# (block 256), from an ncu capture of ``bench.py --kernel adamw8bit --small``
 A8_DRAM_BYTES_PER_ELEMENT = (1.619793e9 + 1.024948e9) / (1 << 28)
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 N_LAYERS, D, KV, FF, VOCAB = 32, 4096, 1024, 14336, 128256
 
 
@@ -430,6 +440,19 @@ def run_ours(args, rank, world, local_rank):
             e2e = dict(e2e_serial, api="opt.step() between host copies", staged_error=staged_error)
         del pin_g, pin_p
 
+    # ---- after the measurements: the reference's GPU path (1 GPU), sharded parity (N > 1) ----
+    del opt
+    torch.cuda.empty_cache()
+    ref_gpu = sharded = None
+    if world == 1 and not args.no_reference_gpu:
+        try:
+            ref_gpu = reference_gpu(args, device, muon, adam)
+        except Exception as exc:  # reported in the line; the engine's numbers above stand
+            ref_gpu = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+        torch.cuda.empty_cache()
+    if world > 1:
+        sharded = sharded_bit_check(device)
+
     result = None
     if rank == 0:
         peak_ns = tf_sus
@@ -452,13 +475,13 @@ def run_ours(args, rank, world, local_rank):
                          "frac": (ns_tflops / peak_ns) if ns_tflops else None,
                          "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None,
                          "traffic_note": "tensor-bound chain of mixed shapes; per-launch DRAM bytes equal the "
-                                         "algorithmic operand bytes (profiles/gemm_pair_kernel_ns_4x4096.md)"},
+                                         "algorithmic operand bytes (ncu capture of bench.py --kernel ns --small)"},
             "roofline_8bit": {"bound": "hbm", "kernel": "adamw8bit_kernel", "achieved": a8_gbs, "peak": hbm_gbs,
                               "unit": "GB/s", "frac": (a8_gbs / hbm_gbs) if a8_gbs else None,
                               "algorithmic_bytes": a8_bytes,
                               "traffic": A8_DRAM_BYTES_PER_ELEMENT * a8_elems_rank,
                               "traffic_note": "DRAM bytes per element of a 2^28-element ncu capture "
-                                              "(profiles/adamw8bit_kernel_256M.md) scaled to the elements "
+                                              "(bench.py --kernel adamw8bit --small) scaled to the elements "
                                               "this rank updates per step, like achieved"},
             "other_configs": extra,
             "gpu_launches": int(launches),
@@ -466,69 +489,292 @@ def run_ours(args, rank, world, local_rank):
             "e2e": e2e,
             "e2e_serial": e2e_serial,
         }
+        if ref_gpu is not None:
+            result["reference_gpu"] = ref_gpu
+        if sharded is not None:
+            result["sharded_bit_identical"] = sharded
     return result
 
 
+def sharded_bit_check(device):
+    """N > 1: the sharded step writes the single-GPU bits. A small hybrid Muon + AdamW step
+    (batch_ns, two steps) and an 8-bit AdamW step run twice from the same weights and
+    gradients on every rank -- once sharded over all ranks (``Sharder``), once unsharded on
+    this rank's GPU -- and every weight is compared bit for bit; the mismatch count is
+    summed over ranks."""
+    from muon_sr_b200 import Sharder, TritonAdamW8bit, TritonMuonSRWithAuxAdam
+    g = torch.Generator().manual_seed(123)
+    mshapes = [(256, 512)] * 6 + [(512, 256)] * 4 + [(384, 384)] * 3 + [(1024, 256)] * 2
+    shapes = mshapes + [(2000, 256), (256,), (256,), (512,)]
+    init = [(torch.randn(shp, generator=g) * 0.02).bfloat16() for shp in shapes]
+    grads = [[(torch.randn(shp, generator=g) * 1e-3).bfloat16().to(device) for shp in shapes] for _ in range(2)]
+    nm = len(mshapes)
+
+    def hybrid(ps, sh):
+        return TritonMuonSRWithAuxAdam([
+            dict(params=ps[:nm], use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+            dict(params=ps[nm:], use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01)],
+            batch_ns=True, shard=sh)
+
+    def eight_bit(ps, sh):
+        return TritonAdamW8bit([dict(params=ps, optim_bits=8)], lr=1e-3, weight_decay=0.01, shard=sh)
+
+    bad = compared = 0
+    for make in (hybrid, eight_bit):
+        pa = [torch.nn.Parameter(t.to(device)) for t in init]
+        pb = [torch.nn.Parameter(t.to(device)) for t in init]
+        oa, ob = make(pa, Sharder()), make(pb, None)
+        for gs in grads:
+            for p, q, gr in zip(pa, pb, gs):
+                p.grad = gr.clone()
+                q.grad = gr.clone()
+            oa.step()
+            ob.step()
+        torch.cuda.synchronize()
+        bad += sum(int(not torch.equal(p.detach().view(torch.int16), q.detach().view(torch.int16)))
+                   for p, q in zip(pa, pb))
+        compared += len(pa)
+        del oa, ob
+    t = torch.tensor([bad], dtype=torch.int64, device=device)
+    dist.all_reduce(t)
+    return {"identical": int(t.item()) == 0, "mismatched_tensors_all_ranks": int(t.item()),
+            "tensors_per_rank": compared,
+            "what": "hybrid Muon+AdamW (batch_ns, 2 steps) and 8-bit AdamW (2 steps), 19 tensors each, "
+                    "sharded over all ranks vs unsharded on each rank"}
+
+
 # ---------------------------------------------------------------------------------------
-# CPU (reference) arm -- the reference's pure-PyTorch MuonSR / AdamW-SR restated in oracle/
+# the reference itself (baseline/_ref): CPU arm, configs[0] on the CPU, GPU path on this GPU
 # ---------------------------------------------------------------------------------------
-CPU_SAMPLE = ("per step: three MuonSR parameter steps (oracle.muon_cpu, restating muon_sr/muon_sr.py) for each "
-              "of the four distinct Llama-3-8B matrix shapes, scaled by that shape's count, plus an AdamW-SR "
-              "step on a 2^23-element slice scaled by elements to the 1.05G-element AdamW group")
+def reference_module():
+    """(the unmodified reference package installed in baseline/_ref, None) or (None, why not)."""
+    if not os.path.isdir(os.path.join(REF_DIR, "muon_sr")):
+        return None, "baseline/_ref is not installed"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import muon_sr
+    except Exception as exc:  # e.g. triton missing: the reference imports it at module load
+        return None, f"importing the reference failed: {type(exc).__name__}: {exc}"[:300]
+    return muon_sr, None
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+CPU_SAMPLE = ("per step: one MuonSRWithAuxAdam(batch_ns=True) step per distinct Llama-3-8B matrix shape (one "
+              "matrix each: q/o 4096x4096, k/v 1024x4096, gate/up 14336x4096, down 4096x14336) scaled by that "
+              "shape's count, plus the AdamW group's step on a 2^22-element slice scaled by elements to the "
+              "1.05G-element AdamW group")
+_cpu_opts = {}
 
 
 def cpu_sample_step(threads):
-    """One bounded sample of the full Llama step on the host cores: MuonSR parameter steps
-    for three matrices of each distinct shape (q/o, k/v, gate/up, down), scaled by that
-    shape's count, and an AdamW-SR step on a 2^23-element slice scaled by elements.
-    Returns (extrapolated milliseconds per full step, seconds of CPU work in the sample)."""
-    from oracle.muon_cpu import adamw_sr_step, muon_sr_step
+    """One bounded sample of the full Llama step on the host cores: the reference's own
+    ``MuonSRWithAuxAdam(batch_ns=True)`` (baseline/_ref; the oracle's restatement if the
+    install is missing) on one matrix of each distinct shape, each timed on its own and scaled
+    by that shape's count, and on an AdamW-group slice scaled by elements. The optimizers are
+    built once and reused, so warm-up steps create their state and timed steps are steady.
+    Returns (extrapolated ms per full step, seconds of CPU work actually timed, kind)."""
     torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(0)
+    ref, _ = reference_module()
     muon_shapes, adam_shapes = llama_shapes()
     counts = {}
-    for s in muon_shapes:
-        counts[s] = counts.get(s, 0) + 1
-    full = 0.0
-    work = 0.0
-    per_shape = 3  # matrices sampled per distinct shape
-    for shape, count in counts.items():
-        for _ in range(per_shape):
-            p = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
-            gr = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
-            b = torch.zeros_like(p)
+    for shp in muon_shapes:
+        counts[shp] = counts.get(shp, 0) + 1
+    n_slice = 1 << 22
+    n_adam = sum(math.prod(shp) for shp in adam_shapes)
+    if not _cpu_opts:
+        g = torch.Generator().manual_seed(0)
+
+        def param(shape):
+            p = torch.nn.Parameter((torch.randn(*shape, generator=g) * 0.02).bfloat16())
+            p.grad = (torch.randn(*shape, generator=g) * 1e-3).bfloat16()
+            return p
+        for shape in counts:
+            p = param(shape)
+            if ref is not None:
+                opt = ref.MuonSRWithAuxAdam([dict(params=[p], use_muon=True, lr=0.02, momentum=0.95,
+                                                  weight_decay=0.01)], batch_ns=True)
+                _cpu_opts[shape] = (opt.step, counts[shape])
+            else:
+                from oracle.muon_cpu import muon_sr_step
+                buf = torch.zeros_like(p)
+                _cpu_opts[shape] = ((lambda p=p, b=buf: muon_sr_step([p], [p.grad], [b], lr=0.02,
+                                                                      weight_decay=0.01)), counts[shape])
+        pa = param((n_slice,))
+        if ref is not None:
+            opt = ref.MuonSRWithAuxAdam([dict(params=[pa], use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10,
+                                              weight_decay=0.01)], batch_ns=True)
+            _cpu_opts["adamw"] = (opt.step, n_adam / n_slice)
+        else:
+            from oracle.muon_cpu import adamw_sr_step
+            ea, eb = torch.zeros_like(pa), torch.zeros_like(pa)
+            _cpu_opts["adamw"] = ((lambda: adamw_sr_step([pa], [pa.grad], [ea], [eb], 1, weight_decay=0.01)),
+                                  n_adam / n_slice)
+    full = work = 0.0
+    for fn, scale in _cpu_opts.values():
+        t0 = time.perf_counter()
+        fn()
+        dt = time.perf_counter() - t0
+        full += dt * scale
+        work += dt
+    return full * 1e3, work, ("reference" if ref is not None else "port")
+
+
+def cpu_reference_configs0(threads):
+    """configs[0] on the host cores, whole and unextrapolated: the reference's ``MuonSR``
+    (baseline/_ref) on the GPT-2-small matrix set -- 12 x {768x2304, 768x768, 768x3072,
+    3072x768} bf16 params N(0, 0.02), grads N(0, 1e-3), momentum 0.95, Nesterov, ns_steps 5,
+    lr 0.02, wd 0.01 -- one warm-up step and the best of 3, with batch_ns False and True."""
+    ref, why = reference_module()
+    if ref is None:
+        return {"unavailable": why}
+    torch.set_num_threads(threads)
+    out = {"cores": threads, "cpu_model": cpu_model(), "unit": "ms", "matrices": 48,
+           "ns_tflop_per_step": 12 * sum(ns_flops(shp) for shp in GPT2_MATS) / 1e12}
+    for batch in (False, True):
+        g = torch.Generator().manual_seed(0)
+        ps = []
+        for _ in range(12):
+            for shp in GPT2_MATS:
+                p = torch.nn.Parameter((torch.randn(*shp, generator=g) * 0.02).bfloat16())
+                p.grad = (torch.randn(*shp, generator=g) * 1e-3).bfloat16()
+                ps.append(p)
+        opt = ref.MuonSR(ps, lr=0.02, weight_decay=0.01, momentum=0.95, nesterov=True, ns_steps=5, batch_ns=batch)
+        opt.step()
+        best = float("inf")
+        for _ in range(3):
             t0 = time.perf_counter()
-            muon_sr_step([p], [gr], [b], lr=0.02, weight_decay=0.01)
-            dt = time.perf_counter() - t0
-            full += dt * count / per_shape
-            work += dt
-    n_slice = 1 << 23
-    pa = (torch.randn(n_slice, generator=g) * 0.02).bfloat16()
-    ga = (torch.randn(n_slice, generator=g) * 1e-3).bfloat16()
-    ea, eb = torch.zeros_like(pa), torch.zeros_like(pa)
-    t0 = time.perf_counter()
-    adamw_sr_step([pa], [ga], [ea], [eb], 1, weight_decay=0.01)
-    dt = time.perf_counter() - t0
-    full += dt * sum(math.prod(s) for s in adam_shapes) / n_slice
-    work += dt
-    return full * 1e3, work
+            opt.step()
+            best = min(best, time.perf_counter() - t0)
+        out[f"batch_ns_{str(batch).lower()}_ms"] = best * 1e3
+    return out
+
+
+GPT2_MATS = ((768, 2304), (768, 768), (768, 3072), (3072, 768))
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's CPU path on the host cores (rank 0 only)."""
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    sample = CPU_SAMPLE
     for _ in range(args.warmup):
         cpu_sample_step(threads)
-    vals = [cpu_sample_step(threads)[0] for _ in range(args.steps)]
-    v = statistics.median(vals)
+    samples = [cpu_sample_step(threads) for _ in range(args.steps)]
+    v = statistics.median(x[0] for x in samples)
+    kind = samples[0][2]
+    timed_s = sum(x[1] for x in samples)
+    sample = CPU_SAMPLE + (" (the reference's own classes from baseline/_ref)" if kind == "reference" else
+                           " (the oracle's restatement: baseline/_ref is not installed)")
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "ms", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "configs[3]: hybrid Muon+AdamW SR step, Llama-3-8B shapes (CPU, sampled)"},
-            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
+            "config": {"workload": "configs[3]: MuonSRWithAuxAdam(batch_ns=True) step, Llama-3-8B shapes, on the "
+                                   "host cores (sampled, extrapolated)"},
+            "extrapolated": True, "cpu_seconds_timed": timed_s,
+            "cpu_baseline": {"value": v, "unit": "ms", "cores": threads, "kind": kind, "sample": sample,
+                             "cpu_model": cpu_model(), "extrapolated": True},
             "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_gpu(args, device, muon, adam):
+    """The reference's own GPU path (baseline/_ref: its Triton kernels and its torch/cuBLAS
+    Newton-Schulz, unmodified, through its public classes) on this GPU, on the same synthetic
+    tensors, next to this engine on the same work. CUDA events on the current stream, the
+    reference's steps after its own warm-up (Triton compiles on the first call)."""
+    ref, why = reference_module()
+    if ref is None:
+        return {"unavailable": why}
+    from muon_sr_b200 import TritonAdamW, TritonAdamW8bit, TritonMuonSR, TritonMuonSRWithAuxAdam, TritonSRAccumulator
+    from muon_sr_b200 import kernels as K
+    from muon_sr.muon_sr import _newton_schulz as ref_ns
+    steps, warm = min(args.steps, 5), 3
+    out = {"steps": steps, "warmup": warm, "unit": "ms", "source": "baseline/_ref (pip install of the reference)"}
+
+    def pair(name, ours_fn, ref_fn, st=steps, wu=warm):
+        o = time_steps(ours_fn, st, wu, 1)
+        r = time_steps(ref_fn, st, wu, 1)
+        out[name] = {"reference_ms": r, "ours_ms": o, "speedup": r / o}
+        torch.cuda.empty_cache()
+
+    groups = lambda m, a: [dict(params=m, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+                           dict(params=a, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01)]
+    # configs[3]: the full hybrid step
+    ours = TritonMuonSRWithAuxAdam(groups(muon, adam), batch_ns=True)
+    theirs = ref.TritonMuonSRWithAuxAdam(groups(muon, adam), batch_ns=True)
+    pair("configs3_hybrid_step", ours.step, theirs.step)
+    del ours, theirs
+    torch.cuda.empty_cache()
+    # configs[2]: 8-bit blockwise AdamW on the same tensors
+    params = muon + adam
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, block_size=256)
+    ours = TritonAdamW8bit([dict(params=params, optim_bits=8)], **kw)
+    theirs = ref.TritonAdamW8bit([dict(params=params, optim_bits=8)], **kw)
+    pair("configs2_adamw8bit_step", ours.step, theirs.step)
+    out["configs2_adamw8bit_step"]["algorithmic_gb"] = (10 * sum(p.numel() for p in params)
+                                                        + 16 * sum(math.ceil(p.numel() / 256) for p in params)) / 1e9
+    del ours, theirs
+    torch.cuda.empty_cache()
+    # configs[4]: one SR-accumulation micro-batch (after the first) through each one's hook
+    grads = [p.grad for p in params]
+
+    def micro(hook):
+        def run():
+            for p, g in zip(params, grads):
+                p.grad = g
+                hook(p)
+        return run
+    for hook in (TritonSRAccumulator._accum_hook, ref.TritonSRAccumulator._accum_hook):
+        micro(hook)()
+        o = time_steps(micro(hook), steps, 1, 1)
+        out.setdefault("configs4_sr_accum_microbatch", {})["ours_ms" if hook is TritonSRAccumulator._accum_hook
+                                                          else "reference_ms"] = o
+        for p, g in zip(params, grads):
+            del p.acc_grad
+            p.grad = g
+    c4 = out["configs4_sr_accum_microbatch"]
+    c4["speedup"] = c4["reference_ms"] / c4["ours_ms"]
+    torch.cuda.empty_cache()
+    # configs[1]: TritonAdamW on the GPT-2 AdamW set; configs[0]'s matrices as a TritonMuonSR step
+    gg = torch.Generator(device=device).manual_seed(1)
+    mk = lambda shp, std: torch.empty(shp, dtype=torch.bfloat16, device=device).normal_(0, std, generator=gg)
+    gpt2 = [torch.nn.Parameter(mk(shp, 0.02)) for shp in [(50257, 768)] + [(768,)] * 24]
+    mats = [torch.nn.Parameter(mk(shp, 0.02)) for _ in range(12) for shp in GPT2_MATS]
+    for p in gpt2 + mats:
+        p.grad = mk(p.shape, 1e-3)
+    kw = dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01)
+    ours, theirs = TritonAdamW(gpt2, **kw), ref.TritonAdamW(gpt2, **kw)
+    pair("configs1_adamw_step", ours.step, theirs.step, st=50, wu=5)
+    ours = TritonMuonSR(mats, lr=0.02, weight_decay=0.01, batch_ns=True)
+    theirs = ref.TritonMuonSR(mats, lr=0.02, weight_decay=0.01, batch_ns=True)
+    pair("configs0_gpt2_muon_step", ours.step, theirs.step, st=20, wu=3)
+    del ours, theirs, gpt2, mats
+    torch.cuda.empty_cache()
+    # Newton-Schulz per shape: the stacks one chunk of each configuration's step holds
+    ns = {}
+    for name, shape in (("q/o", (16, D, D)), ("k/v", (64, KV, D)), ("gate/up", (4, FF, D)), ("down", (4, D, FF)),
+                        ("gpt2 768x2304", (12, 768, 2304)), ("gpt2 768x768", (12, 768, 768)),
+                        ("gpt2 768x3072", (12, 768, 3072)), ("gpt2 3072x768", (12, 3072, 768))):
+        x = torch.empty(shape, dtype=torch.bfloat16, device=device).normal_(0, 1e-3, generator=gg)
+        flops = shape[0] * ns_flops(shape[1:]) / 1e12
+        o = time_steps(lambda: K.newton_schulz(x, 5), steps, warm, 1)
+        r = time_steps(lambda: ref_ns(x, 5, None), steps, warm, 1)
+        ns[name] = {"shape": list(shape), "ours_tflops": flops / (o * 1e-3), "reference_tflops": flops / (r * 1e-3),
+                    "speedup": r / o}
+        del x
+        torch.cuda.empty_cache()
+    out["newton_schulz_effective_tflops"] = ns
+    return out
 
 
 def run_kernel_case(args):
@@ -594,6 +840,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU path (baseline/_ref) next to the engine")
     ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply"],
                     help="time one kernel alone (profiling cases) instead of the optimizer step")
     ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
@@ -623,9 +871,13 @@ def main():
         out = run_ours(args, rank, world, local_rank)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
-                v, secs = cpu_sample_step(os.cpu_count() or 1)
-                out["cpu_baseline"] = {"value": v, "unit": "ms", "cores": os.cpu_count() or 1, "kind": "port",
-                                       "sample": f"{CPU_SAMPLE} ({secs:.1f} s of CPU work)"}
+                threads = os.cpu_count() or 1
+                cpu_sample_step(threads)  # builds the sampled optimizers' state (untimed)
+                v, secs, kind = cpu_sample_step(threads)
+                out["cpu_baseline"] = {"value": v, "unit": "ms", "cores": threads, "kind": kind,
+                                       "cpu_model": cpu_model(), "extrapolated": True,
+                                       "cpu_seconds_timed": secs, "sample": CPU_SAMPLE}
+                out["cpu_reference_configs0"] = cpu_reference_configs0(threads)
             print(json.dumps(out), flush=True)
     finally:
         if world > 1:

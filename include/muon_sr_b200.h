@@ -278,7 +278,9 @@ int msr_newton_schulz_bf16(const void* x, void* out, int64_t batch, int64_t rows
  *   with MSR_ERR_WORKSPACE (e.g. up to a 2048 x 2048 matrix, or 4 of 1024 x 1024).
  * - Every GPU that loads the library holds the 64 MiB area until the process exits.
  * - The first call on a device looks up the area's address on that device; make that first
- *   call before any stream capture.
+ *   call before any stream capture. The address is kept for the life of the process: after
+ *   cudaDeviceReset (or anything else that destroys the device's primary context) it is
+ *   stale, so do not call this function again in that process.
  * - All calls share the one area: calls that overlap on the GPU (other streams, other host
  *   threads without ordering) race and corrupt each other's results. Serialise them. */
 int msr_newton_schulz_bf16_noalloc(const void* x, void* out, int64_t batch, int64_t rows,

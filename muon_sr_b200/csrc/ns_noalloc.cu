@@ -12,6 +12,9 @@
 // on which the library's kernels are loaded holds it until the process exits. Its device
 // address is looked up once per device (cudaGetSymbolAddress, with that device current) on
 // the first call made on that device; host code never uses the array's name as a pointer.
+// The looked-up address is cached for the life of the process; a device reset (which
+// destroys the primary context the address belongs to) is not detected, so callers must not
+// use this entry point again after resetting the device.
 #include "common.cuh"
 #include "host_common.h"
 

@@ -74,6 +74,12 @@ class _Recorder:
         self.size = 0
         self.cursor = 0
         self.seen = 0
+        self.held = []  # scratch tensors the captured kernels use (kept alive with the graph)
+
+    def hold(self, tensor):
+        """Keep ``tensor`` alive as long as the captured graph: its address is baked in."""
+        if not any(t is tensor for t in self.held):
+            self.held.append(tensor)
 
     def constant(self, name, value):
         """A scalar the capture bakes into a kernel's parameters: a refresh must see the same."""
@@ -148,7 +154,7 @@ def _restore(opt, snap):
 
 
 class _Slot:
-    __slots__ = ("graph", "host", "dev", "plan", "constants", "done")
+    __slots__ = ("graph", "host", "dev", "plan", "constants", "done", "held")
 
 
 class StepGraph:
@@ -204,7 +210,7 @@ class StepGraph:
                 raise RuntimeError(_CHANGED)
             self._storage = storage
             pool = s.graph.pool()
-            s.plan, s.constants = rec.plan, rec.constants
+            s.plan, s.constants, s.held = rec.plan, rec.constants, rec.held
             s.done = torch.cuda.Event()
             self._slots.append(s)
         self._next = 0

@@ -204,12 +204,17 @@ _workspaces = {}
 def _workspace(device, nbytes: int) -> torch.Tensor:
     """Scratch buffer for the Newton-Schulz chain, one per (device, stream) and grown on
     demand: calls on one stream reuse it in stream order, calls on different streams never
-    share it."""
+    share it. A buffer used while a ``StepGraph`` captures is also held by that graph's
+    recorder (``hold``), so growing the buffer later for an eager call never returns memory
+    a captured graph still writes to."""
     device = torch.device(device)
     key = (device.index, torch.cuda.current_stream(device).cuda_stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         _workspaces[key] = ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    rec = _recorder()
+    if rec is not None and rec.launches:
+        rec.hold(ws)
     return ws
 
 

@@ -153,6 +153,8 @@ class Sharder:
     def bind(self, optimizer):
         self._ensure(optimizer)
         self._groups = optimizer.param_groups
+        if self.transport == "p2p" and self._p2p and self._p2p.stale():
+            self._p2p = None  # some owner's weights moved: every rank maps them again
         if self.transport == "p2p" and self._p2p is None:
             self._p2p = _PeerMaps(self) if _PeerMaps.possible(self) else False
             if self._p2p is False:
@@ -306,6 +308,7 @@ class _PeerMaps:
         self.lib = _lib.load()
         self.device = torch.device("cuda", torch.cuda.current_device())
         mine = []
+        self.exported = []  # (param, address at export): the peers' mappings point there
         for i, p in enumerate(sh._order):
             if sh._owner[id(p)] == sh.rank:
                 h = ctypes.create_string_buffer(64)
@@ -313,6 +316,7 @@ class _PeerMaps:
                 _lib.check(self.lib.msr_ipc_export(ctypes.c_void_p(p.data_ptr()), h, ctypes.byref(off)),
                            "msr_ipc_export")
                 mine.append((i, bytes(h.raw), off.value))
+                self.exported.append((p, p.data_ptr()))
         lists = [None] * sh.world
         dist.all_gather_object(lists, mine, group=sh._host)
         self.bases = []
@@ -335,6 +339,16 @@ class _PeerMaps:
         self.owned_events = []
         self.events = []      # per share point: (local event, {rank: peer event})
         self.done = self._event_set()
+
+    def stale(self) -> bool:
+        """Collective (host group): True on every rank if any rank's owned parameters no
+        longer live where they were exported (``.to()``, a ``load_state_dict`` that
+        replaced them, re-materialised tensors), so that all ranks rebuild their mappings
+        together instead of copying from stale peer addresses."""
+        moved = any(p.data_ptr() != ptr for p, ptr in self.exported)
+        flag = torch.tensor([1 if moved else 0], dtype=torch.int32)
+        dist.all_reduce(flag, group=self.sh._host)
+        return bool(flag.item())
 
     def _event_set(self):
         """One interprocess event of this rank plus the opened events of every peer."""

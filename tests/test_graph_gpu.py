@@ -52,7 +52,7 @@ def _same(pa, pb, opt_a, opt_b, what):
                 assert sa[k] == sb[k], (what, k, i)
 
 
-def _run(make, shapes, steps=4, random_seeds=False, lr_change=None):
+def _run(make, shapes, steps=4, random_seeds=False, lr_change=None, after_capture=None):
     pa, pb = _twins(shapes)
     opt_a, opt_b = make(pa), make(pb)
     ga, gb = [p.grad for p in pa], [p.grad for p in pb]
@@ -64,6 +64,8 @@ def _run(make, shapes, steps=4, random_seeds=False, lr_change=None):
     _same(pa, pb, opt_a, opt_b, "eager")
     graph = StepGraph(opt_b)
     _same(pa, pb, opt_a, opt_b, "after capture")  # capturing does not step
+    if after_capture is not None:
+        after_capture()
     for step in range(steps):
         _fill(ga, gb, shapes, 200 + step)
         if lr_change is not None and step == 2:
@@ -100,6 +102,44 @@ def test_hybrid_graph_matches_eager(small_chunks, batch_ns):
             dict(params=params[nm:], use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
         ], batch_ns=batch_ns)
     _run(make, MUON + ADAM, lr_change=_halve_lr)
+
+
+def test_graph_keeps_its_workspaces_when_eager_calls_grow_them(small_chunks):
+    """Newton-Schulz scratch a captured graph writes to stays the graph's: after capture, larger
+    eager Newton-Schulz calls on the side streams and on the current stream replace those
+    streams' workspaces; tensors allocated afterwards on the same streams (where the caching
+    allocator would hand out a freed workspace block) must not be touched by the replays, and
+    the replays still give the eager steps' bits."""
+    import muon_sr_b200.kernels as KK
+    nm = len(MUON)
+    fillers = []
+
+    def make(params):
+        return TritonMuonSRWithAuxAdam([
+            dict(params=params[:nm], use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
+            dict(params=params[nm:], use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
+        ], batch_ns=True)
+
+    def grow():
+        dev = torch.device(DEV, torch.cuda.current_device())
+        streams = list(M._side_streams(dev)[0]) + [torch.cuda.current_stream(dev)]
+        big = (torch.randn(2, 512, 768, device=DEV) * 1e-3).bfloat16()
+        for s in streams:
+            s.wait_stream(torch.cuda.current_stream(dev))
+            old = KK._workspaces.get((dev.index, s.cuda_stream))
+            size = old.numel() if old is not None else 1 << 20
+            with torch.cuda.stream(s):
+                KK.newton_schulz(big, 5)     # grows (replaces) this stream's workspace
+                del old
+                for _ in range(4):           # candidates for the freed block
+                    fillers.append(torch.full((size,), 0x5A, dtype=torch.uint8, device=DEV))
+            torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+
+    _run(make, MUON + ADAM, after_capture=grow)
+    torch.cuda.synchronize()
+    for f in fillers:
+        assert bool((f == 0x5A).all()), "a replay wrote into memory the graph no longer owns"
 
 
 def test_random_seed_hybrid_graph_matches_eager(small_chunks):

@@ -293,3 +293,26 @@ def test_centralize_matches_reference_ops(shape):
     bound = ulp + 0.5 * 2.0 ** -18 * row_mag
     assert bool(((got.float() - wf).abs() <= bound).all())
     assert torch.equal(g, g0)  # the gradient itself is not modified
+
+
+def test_muon_prepare_gate_up_matrix_counters_cross_2_32():
+    """One full gate/up matrix (14336 x 4096 = 58.7M elements) at the stack position whose
+    Philox counters run through 2^32 (row 73 of a stack: counters 73 * numel ...), where the
+    reference's int32 offset wraps (muon_sr/triton_muon_sr.py:44,156-164). The oracle checks
+    the elements around the wrap and both ends of the matrix bit for bit."""
+    numel = 14336 * 4096
+    base = 73 * numel
+    assert base < 2**32 < base + numel
+    g = torch.Generator(device=DEV).manual_seed(73)
+    grad = (torch.randn(numel, device=DEV, generator=g) * 1e-3).bfloat16()
+    buf = (torch.randn(numel, device=DEV, generator=g) * 1e-3).bfloat16()
+    b0 = bits_of(buf)
+    upd = torch.empty_like(buf)
+    seed = deterministic_seed(5, 4, 0)
+    K.muon_prepare([(grad, buf, upd, base, seed)], 0.95, True)
+    wrap = 2**32 - base
+    gb, ob, ou = bits_of(grad), bits_of(buf), bits_of(upd)
+    for lo, hi in ((0, 1 << 16), (wrap - (1 << 19), wrap + (1 << 19)), (numel - (1 << 16), numel)):
+        eb, eu = ew.muon_prepare(gb[lo:hi], b0[lo:hi], 0.95, True, seed, ctr_base=base + lo)
+        assert_bits_equal(ob[lo:hi], eb, f"momentum [{lo}, {hi})")
+        assert_bits_equal(ou[lo:hi], eu, f"update [{lo}, {hi})")

@@ -215,3 +215,30 @@ def test_ns_orthogonality_llama_shape():
     s = torch.linalg.svdvals(y[0].float())
     assert float(s.max()) < 1.3 and float(s.min()) > 0.3, (float(s.min()), float(s.max()))
     assert K.device_error() == 0
+
+
+# Every matrix shape of the benchmark configurations: Llama-3-8B (q/o 4096 x 4096, k/v
+# 1024 x 4096, gate/up 14336 x 4096 -- tall, run through the transposed X^T X path -- and
+# down 4096 x 14336) and GPT-2-small (768 x 2304, 768 x 768, 768 x 3072, 3072 x 768).
+CONFIG_SHAPES = [(1, 4096, 4096), (2, 1024, 4096), (1, 14336, 4096), (1, 4096, 14336),
+                 (2, 768, 2304), (2, 768, 768), (2, 768, 3072), (2, 3072, 768)]
+
+
+@pytest.mark.parametrize("shape", CONFIG_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_ns_matches_reference_ops_at_config_shapes(shape):
+    """The engine's chain against the reference's ``_newton_schulz`` (muon_sr/muon_sr.py:82-98)
+    run as torch ops on this GPU, on the inputs a Muon step feeds it (a Nesterov update of
+    N(0, 1e-3) gradients): north-star gate rel. Frobenius <= 1e-2, and with the reference's
+    rounding points and tile-aligned shapes the result is bit-identical to cuBLAS's for
+    (almost) every element -- the fraction is printed and gated."""
+    g = torch.Generator(device=DEV).manual_seed(shape[1] * 3 + shape[2])
+    x = (torch.randn(*shape, device=DEV, generator=g) * 1e-3).bfloat16()
+    y = K.newton_schulz(x, 5)
+    ref = ns_ref(x, 5, None)
+    assert K.device_error() == 0
+    err = rel_frobenius(y, ref)
+    same = (y.view(torch.int16) == ref.view(torch.int16)).float().mean().item()
+    print(f"NS {shape}: rel. Frobenius {err:.3e}, bit-identical fraction {same:.6f}")
+    assert torch.isfinite(y.float()).all()
+    assert err <= NS_TOL, (shape, err)
+    assert err < 1e-3 and same > 0.99, (shape, err, same)
