@@ -395,6 +395,17 @@ def run_ours(args, rank, world, local_rank):
         del opt_a, gpt2
         torch.cuda.empty_cache()
 
+    # ---- N > 1: the gradients' reduce-scatter onto their owners (Sharder.reduce_grads) ----
+    grad_rs = None
+    if world > 1:
+        lay = shard.reduce_grads(opt)  # first call packs the gradients and makes them views (untimed)
+        rs_ms = time_steps(lambda: shard.reduce_grads(opt), 3, 1, world)
+        nbytes = world * lay["chunk_elements"] * 2
+        grad_rs = {"ms": rs_ms, "collective": "one NCCL reduce-scatter (AVG) over the owner-ordered packed bf16 "
+                                              "gradient buffer, in place",
+                   "buffer_bytes": nbytes, "padding": lay["padding"], "tensors": lay["tensors"],
+                   "bus_gbs": nbytes / (rs_ms * 1e-3) / 1e9 * (world - 1) / world}
+
     # ---- end to end through the public API with host buffers ----
     # HostStaging: each step uploads the gradients it reads from pinned host memory and
     # downloads the weights it updates, overlapped with the step chunk by chunk; the step's
@@ -493,6 +504,8 @@ def run_ours(args, rank, world, local_rank):
             result["reference_gpu"] = ref_gpu
         if sharded is not None:
             result["sharded_bit_identical"] = sharded
+        if grad_rs is not None:
+            result["grad_reduce_scatter"] = grad_rs
     return result
 
 
@@ -809,6 +822,10 @@ def run_kernel_case(args):
             m, v = torch.zeros_like(p), torch.zeros_like(p)
             fn = lambda: K.adamw_sr([(p, gr, m, v, 1, 7)], 3e-4, 0.9, 0.95, 1e-10, 0.01)
             work = n * 14 / 1e9
+        elif args.kernel == "accum":
+            acc = torch.empty_like(p).normal_(0, 1e-3, generator=g)
+            fn = lambda: K.grad_accum_(acc, gr, 1234)
+            work = n * 6 / 1e9
         elif args.kernel == "prepare":
             buf, upd = torch.zeros_like(p), torch.empty_like(p)
             fn = lambda: K.muon_prepare([(gr, buf, upd, 0, 7)], 0.95, True)
@@ -842,7 +859,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU path (baseline/_ref) next to the engine")
-    ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply"],
+    ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply", "accum"],
                     help="time one kernel alone (profiling cases) instead of the optimizer step")
     ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
     ap.add_argument("--reserve-sms", type=int, default=int(os.environ.get("MSR_RESERVE_SMS", "0")),

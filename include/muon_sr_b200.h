@@ -119,6 +119,18 @@ typedef struct msr_prepare_entry {
 int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta,
                      int nesterov, msr_stream_t stream);
 
+/* ---- Multicast weights (sharded steps; no counterpart in the single-device reference) ----
+ * The weight-updating entries below (apply, AdamW, 8-bit AdamW) carry `param_mc`: NULL, or
+ * the NVLink multicast address of `param` -- the same offset in a symmetric allocation that
+ * every rank of the node maps and that is bound to one multicast object. With it, the kernel
+ * stores the updated weight once through that address (multimem.st, 16-byte vectors) and
+ * the NVSwitch writes it into every rank's replica, its own included: the update and the
+ * weight all-gather are one kernel. The weight is still read from `param` (this rank's
+ * replica). Requirements: `param_mc` 16-byte aligned like `param`, and when numel is odd the
+ * element after the last one is padding nobody reads (a ragged end is stored in 4-byte
+ * pairs). Readers on other ranks must be ordered after the writing kernel (a device barrier
+ * across the ranks); each CTA ends its multicast stores with a system-scope fence. */
+
 /* ---- Muon apply ----------------------------------------------------------------------
  * Per entry: param[i] <- SR_bf16(float(param[i]) * decay - lr * (float(update[i]) * scale)),
  * counter i, with decay = fp32(1 - lr * weight_decay) computed by the caller in double.
@@ -130,6 +142,7 @@ typedef struct msr_apply_entry {
   uint64_t key;
   float scale;         /* sqrt(max(1, rows/cols)) of the parameter's shape */
   float reserved;
+  void* param_mc;      /* NULL or the multicast address of param (see above) */
 } msr_apply_entry;
 
 int msr_muon_apply(const msr_apply_entry* entries, int count, float lr, float decay, msr_stream_t stream);
@@ -150,6 +163,7 @@ typedef struct msr_adamw_entry {
   uint64_t key_m, key_v, key_p;
   float step_size;
   float bc2_sqrt;
+  void* param_mc;      /* NULL or the multicast address of param (see "Multicast weights") */
 } msr_adamw_entry;
 
 typedef struct msr_adamw_hparams {
@@ -222,6 +236,7 @@ typedef struct msr_adamw8bit_entry {
   float sqrt_bc2_eps;
   int32_t quantized;
   int32_t reserved;
+  void* param_mc;      /* NULL or the multicast address of param (see "Multicast weights") */
 } msr_adamw8bit_entry;
 
 typedef struct msr_adamw8bit_hparams {

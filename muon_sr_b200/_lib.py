@@ -26,13 +26,13 @@ class PrepareEntry(ctypes.Structure):
 
 class ApplyEntry(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("update", c_void_p), ("numel", c_int64), ("key", c_uint64),
-                ("scale", c_float), ("reserved", c_float)]
+                ("scale", c_float), ("reserved", c_float), ("param_mc", c_void_p)]
 
 
 class AdamWEntry(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
                 ("numel", c_int64), ("key_m", c_uint64), ("key_v", c_uint64), ("key_p", c_uint64),
-                ("step_size", c_float), ("bc2_sqrt", c_float)]
+                ("step_size", c_float), ("bc2_sqrt", c_float), ("param_mc", c_void_p)]
 
 
 class AdamWHparams(ctypes.Structure):
@@ -56,7 +56,7 @@ class Adam8Entry(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("state1", c_void_p), ("state2", c_void_p),
                 ("absmax1", c_void_p), ("absmax2", c_void_p), ("numel", c_int64), ("key_p", c_uint64),
                 ("key_m", c_uint64), ("key_v", c_uint64), ("coef", c_float), ("sqrt_bc2_eps", c_float),
-                ("quantized", c_int32), ("reserved", c_int32)]
+                ("quantized", c_int32), ("reserved", c_int32), ("param_mc", c_void_p)]
 
 
 class Adam8Hparams(ctypes.Structure):

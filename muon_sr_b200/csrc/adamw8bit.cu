@@ -32,6 +32,7 @@ struct Adam8Args {
   msr_adamw8bit_hparams hp;
   const float* qmap1;
   const float* qmap2;
+  int any_mc;  // some entry stores its weights through a multicast address
 };
 
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
@@ -255,14 +256,23 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
       }
     }
 
+    uint16_t* PM = static_cast<uint16_t*>(E.param_mc);  // multicast weights (sharded steps)
     if (vec) {
 #pragma unroll
       for (int h = 0; h < EPT; h += 8) {
         U16x8 t;
 #pragma unroll
         for (int j = 0; j < 8; ++j) t.v[j] = pb[h + j];
-        st_u16x8(P + base + h, t);
+        if (PM)
+          mc_st_u16x8(PM + base + h, t);
+        else
+          st_u16x8(P + base + h, t);
       }
+    } else if (PM) {  // 4-byte pairs from an even index; past the end: 0 into the slot's padding
+#pragma unroll
+      for (int j = 0; j < EPT; j += 2)
+        if (base + j < n)
+          mc_st_u32(PM + base + j, pb[j] | (static_cast<uint32_t>(base + j + 1 < n ? pb[j + 1] : 0) << 16));
     } else {
 #pragma unroll
       for (int j = 0; j < EPT; ++j)
@@ -348,6 +358,8 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
       }
     }
   }
+  // multicast stores are ordered before anything after the kernel (the callers' barrier)
+  if (a.any_mc) __threadfence_system();
 }
 
 template <int BS, bool TABLES, int NOISE>
@@ -356,9 +368,9 @@ int launch_variant(const Adam8Args& a, int64_t tiles, cudaStream_t s) {
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
   constexpr size_t smem = smem_for(TABLES);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(adamw8bit_kernel<BS, TABLES, NOISE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (int st = set_smem_attr(reinterpret_cast<const void*>(adamw8bit_kernel<BS, TABLES, NOISE>), smem,
+                               "adamw8bit_kernel"))
+      return st;
   }
   adamw8bit_kernel<BS, TABLES, NOISE><<<grid, Q_THREADS, smem, s>>>(a);
   return check_launch("adamw8bit_kernel");
@@ -408,6 +420,9 @@ extern "C" int msr_adamw8bit(const msr_adamw8bit_entry* entries, int count, cons
       if (e.numel == 0) continue;
       any_quant |= e.quantized != 0;
       a.e[a.count] = e;
+      if (e.param_mc && (reinterpret_cast<uintptr_t>(e.param_mc) & 15u) != (reinterpret_cast<uintptr_t>(e.param) & 15u))
+        return fail(MSR_ERR_INVALID, "msr_adamw8bit: entry %d: param_mc must have param's 16-byte alignment", i);
+      a.any_mc |= e.param_mc != nullptr;
       const unsigned sa = e.quantized ? 8u : 16u;
       a.vec[a.count] = al(e.param, 16) && al(e.grad, 16) && al(e.state1, sa) && al(e.state2, sa);
       a.prefix[a.count] = tiles;

@@ -187,6 +187,20 @@ __device__ __forceinline__ void st_u16x8(void* p, const U16x8& x) {
   *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(x.v);
 }
 
+// Stores through an NVLink multicast address (multimem.st): the bytes land at the same offset
+// in every GPU's memory bound to the multicast object. 16 bytes (8 bf16, moved as four
+// 32-bit words; a store does no arithmetic on them) or 4 bytes (two bf16).
+__device__ __forceinline__ void mc_st_u16x8(void* mc, const U16x8& x) {
+  const uint4 r = *reinterpret_cast<const uint4*>(x.v);
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void mc_st_u32(void* mc, uint32_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.b32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

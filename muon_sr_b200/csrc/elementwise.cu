@@ -124,10 +124,11 @@ struct AccumPolicy {
       o.v[j] = accum_one<NOISE>(va.v[j], vg.v[j], FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
     st_u16x8(a.acc + idx, o);
   }
-  __device__ void scalar(int, int64_t i) const {
+  __device__ void scalar_range(int, int64_t lo, int64_t hi) const {
     const SrNoise<NOISE> nz{a.key};
-    a.acc[i] = accum_one<NOISE>(a.acc[i], a.g[i], nz.at(static_cast<uint64_t>(i)));
+    for (int64_t i = lo; i < hi; ++i) a.acc[i] = accum_one<NOISE>(a.acc[i], a.g[i], nz.at(static_cast<uint64_t>(i)));
   }
+  __device__ bool multicast() const { return false; }
 };
 
 template <int NOISE>
@@ -206,19 +207,22 @@ struct PreparePolicy {
     st_u16x8(static_cast<uint16_t*>(E.momentum) + idx, ob);
     st_u16x8(static_cast<uint16_t*>(E.update) + idx, ou);
   }
-  __device__ void scalar(int e, int64_t i) const {
+  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
     const msr_prepare_entry& E = entry_of<REC>(a, e);
     const SrNoise<NOISE> nz{make_key(E.key)};
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* mb = static_cast<uint16_t*>(E.momentum);
     uint16_t* up = static_cast<uint16_t*>(E.update);
     const bool nesterov = (REC ? a.rec->nesterov : a.nesterov) != 0;
-    uint16_t ob, ou;
-    prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov,
-                       [&] { return nz.at(E.ctr_base + static_cast<uint64_t>(i)); }, ob, ou);
-    mb[i] = ob;
-    up[i] = ou;
+    for (int64_t i = lo; i < hi; ++i) {
+      uint16_t ob, ou;
+      prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov,
+                         [&] { return nz.at(E.ctr_base + static_cast<uint64_t>(i)); }, ob, ou);
+      mb[i] = ob;
+      up[i] = ou;
+    }
   }
+  __device__ bool multicast() const { return false; }
 };
 
 template <int NOISE, bool REC>
@@ -238,6 +242,7 @@ struct ApplyArgs {
   float lr, decay;
   const msr_apply_record* rec;  // msr_muon_apply_rec (see PrepareArgs)
   int32_t src[MAXE];
+  int any_mc;  // some entry stores through a multicast address
 };
 
 template <bool REC>
@@ -284,15 +289,32 @@ struct ApplyPolicy {
     for (int j = 0; j < EW_VEC; ++j)
       o.v[j] = apply_one<NOISE>(vp.v[j], vu.v[j], scale, lr, decay,
                                 FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
-    st_u16x8(static_cast<uint16_t*>(E.param) + idx, o);
+    if (E.param_mc)
+      mc_st_u16x8(static_cast<uint16_t*>(E.param_mc) + idx, o);
+    else
+      st_u16x8(static_cast<uint16_t*>(E.param) + idx, o);
   }
-  __device__ void scalar(int e, int64_t i) const {
+  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
     const msr_apply_entry& E = entry_of<REC>(a, e);
     const SrNoise<NOISE> nz{make_key(E.key)};
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* u = static_cast<const uint16_t*>(E.update);
-    p[i] = apply_one<NOISE>(p[i], u[i], E.scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
+    auto one = [&](int64_t i) {
+      return apply_one<NOISE>(p[i], u[i], E.scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
+    };
+    if (!E.param_mc) {
+      for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
+      return;
+    }
+    // multicast: 4-byte pairs from an even index (lo is a multiple of 8); a pair past the
+    // last element writes 0 into the slot's padding
+    uint16_t* mc = static_cast<uint16_t*>(E.param_mc);
+    for (int64_t i = lo; i < hi; i += 2) {
+      const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
+      mc_st_u32(mc + i, v0 | (v1 << 16));
+    }
   }
+  __device__ bool multicast() const { return a.any_mc != 0; }
 };
 
 template <int NOISE, bool REC>
@@ -312,6 +334,7 @@ struct AdamWArgs {
   msr_adamw_hparams hp;
   const msr_adamw_record* rec;  // msr_adamw_sr_rec (see PrepareArgs)
   int32_t src[MAXE];
+  int any_mc;  // some entry stores through a multicast address
 };
 
 template <bool REC>
@@ -388,25 +411,40 @@ struct AdamWPolicy {
                      "+r"(np_.key.k0), "+r"(np_.key.k1) : "r"(om), "r"(ov), "r"(op));
       }
     }
-    st_u16x8(static_cast<uint16_t*>(E.param) + idx, vp);
+    if (E.param_mc)
+      mc_st_u16x8(static_cast<uint16_t*>(E.param_mc) + idx, vp);
+    else
+      st_u16x8(static_cast<uint16_t*>(E.param) + idx, vp);
     st_u16x8(static_cast<uint16_t*>(E.exp_avg) + idx, vm);
     st_u16x8(static_cast<uint16_t*>(E.exp_avg_sq) + idx, vv);
   }
-  __device__ void scalar(int e, int64_t i) const {
+  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
     const msr_adamw_entry& E = entry_of<REC>(a, e);
     const SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
     uint16_t* p = static_cast<uint16_t*>(E.param);
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
     uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
-    uint16_t pb = p[i], mb = m[i], vb = v[i];
-    const uint64_t c = static_cast<uint64_t>(i);
-    adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), E.step_size, E.bc2_sqrt,
-                     [&](int w) { return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c); });
-    p[i] = pb;
-    m[i] = mb;
-    v[i] = vb;
+    auto one = [&](int64_t i) {
+      uint16_t pb = p[i], mb = m[i], vb = v[i];
+      const uint64_t c = static_cast<uint64_t>(i);
+      adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), E.step_size, E.bc2_sqrt,
+                       [&](int w) { return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c); });
+      m[i] = mb;
+      v[i] = vb;
+      return pb;
+    };
+    if (!E.param_mc) {
+      for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
+      return;
+    }
+    uint16_t* mc = static_cast<uint16_t*>(E.param_mc);  // pairs, as in ApplyPolicy
+    for (int64_t i = lo; i < hi; i += 2) {
+      const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
+      mc_st_u32(mc + i, v0 | (v1 << 16));
+    }
   }
+  __device__ bool multicast() const { return a.any_mc != 0; }
 };
 
 template <int NOISE, bool REC>
@@ -477,18 +515,11 @@ inline bool record_ok(const void* rec) { return rec != nullptr && (reinterpret_c
 
 // Launch of one streamed kernel instance: persistent grid of MINB CTAs per SM (at most one
 // CTA per tile), the ring in dynamic shared memory (the size attribute is set once per
-// device for each instance).
+// device for each kernel function, see set_smem_attr).
 template <int NIN, int S, int MINB, class Args>
 int launch_streamed(void (*kern)(Args, int*), const Args& a, int64_t tiles, cudaStream_t st, const char* name) {
   constexpr size_t smem = stream::smem_bytes<NIN, S>();
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", name, cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
+  if (int status = set_smem_attr(reinterpret_cast<const void*>(kern), smem, name)) return status;
   const int64_t cap = static_cast<int64_t>(sm_count()) * MINB;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
   kern<<<grid, stream::THREADS, smem, st>>>(a, device_error_word());
@@ -553,6 +584,9 @@ int apply_launch(const msr_apply_entry* entries, int count, float lr, float deca
       if (e.numel == 0) continue;
       a.e[a.count] = e;
       a.src[a.count] = i;
+      if (e.param_mc && (reinterpret_cast<uintptr_t>(e.param_mc) & 15u) != (reinterpret_cast<uintptr_t>(e.param) & 15u))
+        return fail(MSR_ERR_INVALID, "msr_muon_apply: entry %d: param_mc must have param's 16-byte alignment", i);
+      a.any_mc |= e.param_mc != nullptr;
       a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.update);
       a.prefix[a.count] = tiles;
       tiles += (e.numel + TILE - 1) / TILE;
@@ -589,6 +623,9 @@ int adamw_launch(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
       if (e.numel == 0) continue;
       a.e[a.count] = e;
       a.src[a.count] = i;
+      if (e.param_mc && (reinterpret_cast<uintptr_t>(e.param_mc) & 15u) != (reinterpret_cast<uintptr_t>(e.param) & 15u))
+        return fail(MSR_ERR_INVALID, "msr_adamw_sr: entry %d: param_mc must have param's 16-byte alignment", i);
+      a.any_mc |= e.param_mc != nullptr;
       a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.grad) && ptr_aligned16(e.exp_avg) &&
                        ptr_aligned16(e.exp_avg_sq);
       a.prefix[a.count] = tiles;

@@ -5,6 +5,9 @@
 #include <string.h>
 
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace msr {
 
@@ -41,6 +44,20 @@ int sm_count() {
   return cached[dev];
 }
 
+int set_smem_attr(const void* func, size_t bytes, const char* name) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "%s: cudaGetDevice: %s", name, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({func, dev})) return MSR_OK;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return fail(MSR_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", name, cudaGetErrorString(e));
+  done.insert({func, dev});
+  return MSR_OK;
+}
+
 int require_sm100() {
   int dev = 0, major = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -54,7 +71,7 @@ int require_sm100() {
 
 extern "C" {
 
-int msr_abi_version(void) { return 1; }
+int msr_abi_version(void) { return 2; }
 
 int msr_set_sr_noise(int mode) {
   if (mode != MSR_SR_NOISE_REFERENCE && mode != MSR_SR_NOISE_FAST && mode != MSR_SR_NOISE_NONE)

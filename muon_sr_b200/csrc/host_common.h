@@ -23,6 +23,10 @@ int require_sm100();
 
 inline cudaStream_t to_stream(msr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize of kernel function `func` to `bytes`,
+// once per (function, device); returns an MSR status.
+int set_smem_attr(const void* func, size_t bytes, const char* name);
+
 // Device address of the library's device error word on the current device (what
 // msr_device_error reads), for kernels that record a wait that ran out; nullptr if unknown.
 int* device_error_word();

@@ -89,7 +89,8 @@ struct TileRef {
 //   int count() const; const int64_t* prefix() const;   (tiles per entry, exclusive prefix)
 //   bool vec(int e) const;  int64_t numel(int e) const;  const void* input(int e, int i) const;
 //   void vector8(int e, int64_t idx, const uint16_t* const (&in)[NIN]) const;   8 elements from smem
-//   void scalar(int e, int64_t i) const;                                        1 element from global
+//   void scalar_range(int e, int64_t lo, int64_t hi) const;   elements lo..hi-1 (< 8) from global
+//   bool multicast() const;   the launch stores through multicast addresses (a system fence ends it)
 template <class Policy, int S>
 __device__ __forceinline__ void run(const Policy& P, Smem<Policy::NIN, S>& sm, int* err) {
   constexpr int NIN = Policy::NIN;
@@ -166,13 +167,16 @@ __device__ __forceinline__ void run(const Policy& P, Smem<Policy::NIN, S>& sm, i
 #pragma unroll
       for (int i = 0; i < NIN; ++i) in[i] = sm.data[s][i] + off;
       P.vector8(r.entry, r.base + off, in);
-    } else {
-      for (int64_t j = off; j < off + EPT && j < r.count; ++j) P.scalar(r.entry, r.base + j);
+    } else if (off < r.count) {
+      P.scalar_range(r.entry, r.base + off, r.base + (off + EPT < r.count ? off + EPT : r.count));
     }
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(&sm.empty[s]);
     if (++s == S) { s = 0; phase ^= 1u; }
   }
+  // multicast stores are ordered before anything this thread does after the kernel (the
+  // callers' cross-rank barrier)
+  if (P.multicast()) __threadfence_system();
 }
 
 }  // namespace stream

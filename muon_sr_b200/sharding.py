@@ -217,29 +217,64 @@ class Sharder:
 
     def reduce_grads(self, optimizer, average: bool = True):
         """Collective replacing the data-parallel gradient all-reduce: every parameter's
-        gradient is summed (or averaged) over the ranks onto its owner only, one bucket per
-        owner, which moves half the bytes of an all-reduce. Non-owners keep their local
-        gradients (the step skips their parameters but still sees that they have one).
-        Every rank calls it after backward with the same parameters holding gradients."""
+        gradient is summed (or averaged) over the ranks onto its owner only, with ONE
+        reduce-scatter per step over an owner-ordered packed gradient buffer -- half the
+        bytes an all-reduce moves. The buffer holds rank r's parameters in chunk r (chunks
+        padded to the largest one, slots aligned to 128 bytes); on the first call each
+        gradient is copied into its slot and ``p.grad`` becomes a view of that slot, so later
+        backward passes that accumulate into the existing ``.grad`` write straight into the
+        buffer and need no copy (a gradient that was replaced, e.g. after
+        ``zero_grad(set_to_none=True)``, is copied in again). Non-owners keep their local
+        gradients (the step skips their parameters but still sees that they have one). Every
+        rank calls it after backward with the same parameters holding gradients. Returns the
+        packed buffer's layout: ``{"chunk_elements", "padding", "tensors"}``."""
         self._ensure(optimizer)
-        for r in range(self.world):
-            grads = [p.grad for p in self._order if p.grad is not None and self._owner[id(p)] == r]
-            if not grads:
-                continue
-            flat = torch.cat([g.reshape(-1) for g in grads])
-            op = dist.ReduceOp.SUM
-            if average and dist.get_backend(self.group) == "nccl":
-                op = dist.ReduceOp.AVG
-            dist.reduce(flat, dst=self._src(r), op=op, group=self.group)
-            if r != self.rank:
-                continue
-            if average and op == dist.ReduceOp.SUM:
-                flat.div_(self.world)
-            off = 0
-            for g in grads:
-                n = g.numel()
-                g.copy_(flat[off:off + n].view_as(g))
-                off += n
+        params = [p for p in self._order if p.grad is not None]
+        if not params:
+            return None
+        key = tuple((id(p), p.numel(), p.grad.dtype, p.grad.device, self._owner[id(p)]) for p in params)
+        lay = getattr(self, "_grad_layout", None)
+        if lay is None or lay["key"] != key:
+            lay = self._grad_layout = self._pack_layout(params, key)
+        buf, chunk = lay["buffer"], lay["chunk"]
+        for p, off in lay["slots"]:
+            view = buf[off:off + p.numel()].view_as(p)
+            if p.grad.data_ptr() != view.data_ptr():
+                view.copy_(p.grad)
+                p.grad = view
+        own = buf[self.rank * chunk:(self.rank + 1) * chunk]
+        if dist.get_backend(self.group) == "nccl":
+            # in place: the output is this rank's chunk of the input
+            dist.reduce_scatter_tensor(own, buf, op=dist.ReduceOp.AVG if average else dist.ReduceOp.SUM,
+                                       group=self.group)
+        else:  # gloo (CPU tests) has no reduce-scatter: the same result through an all-reduce
+            total = buf.clone()
+            dist.all_reduce(total, group=self.group)
+            mine = total[self.rank * chunk:(self.rank + 1) * chunk]
+            own.copy_(mine / self.world if average else mine)
+        return {"chunk_elements": chunk, "padding": lay["padding"], "tensors": len(params)}
+
+    def _pack_layout(self, params, key):
+        """Owner-ordered slots of the packed gradient buffer (same on every rank)."""
+        align = 64  # elements: 128-byte slots keep every gradient 16-byte aligned
+        per_rank = [[] for _ in range(self.world)]
+        for p in params:
+            per_rank[self._owner[id(p)]].append(p)
+        sizes = []
+        for lst in per_rank:
+            sizes.append(sum((p.numel() + align - 1) // align * align for p in lst))
+        chunk = max(align, max(sizes))
+        slots = []
+        for r, lst in enumerate(per_rank):
+            off = r * chunk
+            for p in lst:
+                slots.append((p, off))
+                off += (p.numel() + align - 1) // align * align
+        g0 = params[0].grad
+        buf = torch.zeros(self.world * chunk, dtype=g0.dtype, device=g0.device)
+        used = sum(p.numel() for p in params)
+        return {"key": key, "buffer": buf, "chunk": chunk, "slots": slots,
+                "padding": 1.0 - used / (self.world * chunk)}
 
     # -- checkpoints -----------------------------------------------------------------------
     def gather_state(self, optimizer, dst=None):

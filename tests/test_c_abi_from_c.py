@@ -57,5 +57,5 @@ def test_header_compiles_as_c_and_links(tmp_path):
     numbers, status = run.stdout.strip().split("|")
     version, mode, tiles, count = (int(v) for v in numbers.split())
     # 2 matrices x the upper-triangle pair tiles of a 300 x 300 output (2 x 2 tiles: 3 of them)
-    assert (version, mode, tiles, count) == (1, 2, 6, len(names))
+    assert (version, mode, tiles, count) == (2, 2, 6, len(names))
     assert status == "invalid argument"

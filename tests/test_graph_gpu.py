@@ -182,3 +182,67 @@ def test_graph_argument_errors():
         StepGraph(TritonAdamW8bit([p]))
     with pytest.raises(RuntimeError, match="eager"):
         StepGraph(TritonMuonSR([p]))
+
+
+@pytest.mark.parametrize("batch_ns,fname", [(True, "traj_hybrid_batch.npz"), (False, "traj_hybrid_nobatch.npz")])
+def test_graph_replays_follow_reference_trajectory(batch_ns, fname):
+    """Replayed steps against the reference's own hybrid trajectories (golden vectors from
+    muon_sr's TritonMuonSRWithAuxAdam, muon_sr/triton_muon_sr.py:258-373): step 0 runs eagerly
+    (a capture needs one), steps 1 and 3 are replays of the captured graph, step 2 -- where two
+    parameters have no gradient, a structure the graph refuses -- runs eagerly. Every step is
+    checked with the eager trajectory test's gates (momentum, AdamW tensors and step counters
+    bit-exact)."""
+    from tests._golden import bits_of, load, to_bf16
+    from tests.test_optim_gpu import check_hybrid_step, hybrid_from_golden
+    d = load(fname)
+    params, opt = hybrid_from_golden(d, batch_ns)
+    grads = [torch.empty_like(p) for p in params]  # the tensors behind .grad, kept for the replays
+    graph = None
+    replays = 0
+    for step in range(4):
+        mine_prev = [bits_of(p).ravel() for p in params]
+        full = all(d[f"g{step}_{i}"].size for i in range(len(params)))
+        for i, p in enumerate(params):
+            g = d[f"g{step}_{i}"]
+            if g.size:
+                grads[i].copy_(to_bf16(g, DEV).view(p.shape))
+                p.grad = grads[i]
+            else:
+                p.grad = None
+        if graph is not None and full:
+            graph.step()
+            replays += 1
+        else:
+            opt.step()
+        torch.cuda.synchronize()
+        check_hybrid_step(d, step, params, opt, mine_prev)
+        if graph is None:
+            graph = StepGraph(opt)
+    assert replays == 2
+
+
+def test_graph_adamw_replays_follow_reference_trajectory():
+    """TritonAdamW with centralisation (muon_sr/triton_adamw.py:130-203): step 0 eager, steps 1
+    and 2 replayed, each against the reference's golden trajectory (1 ulp on < 5% of elements,
+    as the eager test allows for the fp32 mean's last bit)."""
+    from tests._golden import bits_of, load, to_bf16
+    from tests.test_optim_gpu import _ulp_diff
+    d = load("traj_adamw_central.npz")
+    shapes = [(12, 20), (20,)]
+    params = [torch.nn.Parameter(to_bf16(d[f"init_{i}"], DEV).view(*s)) for i, s in enumerate(shapes)]
+    grads = [torch.empty_like(p) for p in params]
+    opt = TritonAdamW(params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, centralization=0.5)
+    graph = None
+    for step in range(3):
+        for i, p in enumerate(params):
+            grads[i].copy_(to_bf16(d[f"g{step}_{i}"], DEV).view(p.shape))
+            p.grad = grads[i]
+        (graph.step if graph is not None else opt.step)()
+        torch.cuda.synchronize()
+        for i, p in enumerate(params):
+            for got, want in ((bits_of(p), d[f"p{step}_{i}"]), (bits_of(opt.state[p]["ema"]), d[f"ema{step}_{i}"])):
+                ud = _ulp_diff(got.ravel(), want.ravel())
+                assert ud.max() <= 1.0 + 1e-9 and (ud > 0).mean() < 0.05, (step, i, ud.max())
+        if graph is None:
+            graph = StepGraph(opt)
+

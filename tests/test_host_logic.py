@@ -1,4 +1,5 @@
 """Host-side logic that needs no GPU: seeds, Philox keys, the sharding plan, API errors."""
+import ctypes
 import os
 
 import numpy as np
@@ -179,9 +180,27 @@ def _state_worker(rank, world, port, out):
 
         for i, p in enumerate(order):
             p.grad = torch.full(p.shape, float(rank + 1 + i % 7), dtype=torch.bfloat16)
-        sh.reduce_grads(opt)
+        lay = sh.reduce_grads(opt)
         ok_red = all(bool((p.grad.float() == ((i % 7) + 1.5 if owner[i] == rank else rank + 1 + i % 7)).all())
                      for i, p in enumerate(order))
+        # the gradients are now views of the packed buffer: a backward pass accumulating into
+        # them (here: an in-place fill) needs no copy; a replaced gradient is copied in again
+        buf_ptr = sh._grad_layout["buffer"].data_ptr()
+        ok_red &= all(buf_ptr <= p.grad.data_ptr() < buf_ptr + sh._grad_layout["buffer"].numel() * 2 for p in order)
+        for i, p in enumerate(order):
+            if i == 0:
+                p.grad = torch.full(p.shape, float(2 * rank + 3), dtype=torch.bfloat16)
+            else:
+                p.grad.fill_(float(3 * rank + i % 5))
+        sh.reduce_grads(opt)
+
+        def local(r, i):
+            return 2 * r + 3 if i == 0 else 3 * r + i % 5
+
+        def want(i):
+            return (local(0, i) + local(1, i)) / 2 if owner[i] == rank else local(rank, i)
+        ok_red &= all(bool((p.grad.float() == want(i)).all()) for i, p in enumerate(order))
+        ok_red &= lay["tensors"] == len(order) and 0.0 <= lay["padding"] < 1.0
         out.put((rank, ok_all, ok_dst, ok_red, keys, sorted(set(owner))))
     finally:
         dist.destroy_process_group()
@@ -368,7 +387,8 @@ def test_step_graph_record_refresh():
     arr = (_lib.ApplyEntry * 2)()
     arr[0].numel, arr[1].numel = 10, 20
     m.launch("msr_muon_apply_rec", _lib.ApplyRecord(0.5, 0.9, 2, 0), arr, None)
-    assert m.size == 16 + 2 * 40 and len(m.plan) == 1
+    esz = ctypes.sizeof(_lib.ApplyEntry)
+    assert m.size == 16 + 2 * esz and len(m.plan) == 1
     host = torch.zeros(m.size, dtype=torch.uint8)
     cap = (_lib.ApplyEntry * 2)()
     cap[0].param, cap[0].update, cap[0].numel = 0x1000, 0x3000, 10
@@ -382,7 +402,7 @@ def test_step_graph_record_refresh():
     assert r.complete()
     raw = host.numpy().tobytes()
     hdr = _lib.ApplyRecord.from_buffer_copy(raw[:16])
-    ents = (_lib.ApplyEntry * 2).from_buffer_copy(raw[16:96])
+    ents = (_lib.ApplyEntry * 2).from_buffer_copy(raw[16:16 + 2 * esz])
     assert (hdr.lr, hdr.count) == (0.25, 2)
     assert [(e.param, e.update, e.numel, e.key, e.scale) for e in ents] == \
         [(0x1000, 0x3000, 10, 7, 1.5), (0x2000, 0x4000, 20, 8, 2.0)]

@@ -29,9 +29,8 @@ def _ulp_diff(a_bits, b_bits):
     return np.abs(a - b) / ulp
 
 
-@pytest.mark.parametrize("batch_ns,fname", [(True, "traj_hybrid_batch.npz"), (False, "traj_hybrid_nobatch.npz")])
-def test_hybrid_trajectory(batch_ns, fname):
-    d = load(fname)
+def hybrid_from_golden(d, batch_ns):
+    """The golden hybrid trajectories' parameters (bf16, on the GPU) and optimizer."""
     shapes = MUON_SHAPES + ADAM_SHAPES
     params = [torch.nn.Parameter(to_bf16(d[f"init_{i}"], DEV).view(*s)) for i, s in enumerate(shapes)]
     mp, ap = params[:6], params[6:]
@@ -39,38 +38,51 @@ def test_hybrid_trajectory(batch_ns, fname):
         dict(params=mp, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
         dict(params=ap, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
     ], batch_ns=batch_ns)
+    return params, opt
+
+
+def check_hybrid_step(d, step, params, opt, mine_prev):
+    """One step of the golden hybrid trajectory: step counters, momentum and AdamW tensors
+    and AdamW weights bit-exact; Muon weights within the gate below."""
+    for i, p in enumerate(params):
+        st = opt.state[p]
+        assert int(st.get("step", -1)) == int(d[f"step{step}_{i}"]), ("step", step, i)
+        for key in ("momentum_buffer", "ema", "ema_squared"):
+            k = f"{key}{step}_{i}"
+            if k in d:
+                assert_bits_equal(bits_of(st[key]).ravel(), d[k].ravel(), f"{key} step {step} param {i}")
+        want = d[f"p{step}_{i}"].ravel()
+        got = bits_of(p).ravel()
+        if i >= 6:
+            assert_bits_equal(got, want, f"AdamW param {i} step {step}")
+        else:
+            # The golden run's prepare went through the Triton interpreter, whose
+            # fp32->bf16 cast truncates instead of rounding, so its Newton-Schulz input
+            # differs from the compiled path by up to one bf16 ulp per element; the
+            # quintic iteration amplifies that to a few percent of the update. Gate: the
+            # applied update agrees with the reference's to within 25% in rel. Frobenius
+            # (exact Muon parity is in test_muon_batch_step_matches_oracle_pipeline).
+            prev = d[f"p{step - 1}_{i}"] if step else d[f"init_{i}"]
+            up_mine = bf16_to_f32(got).astype(np.float64) - bf16_to_f32(prev.ravel())
+            up_ref = bf16_to_f32(want).astype(np.float64) - bf16_to_f32(prev.ravel())
+            if not np.any(up_ref):
+                assert_bits_equal(got, mine_prev[i], f"param {i} without a gradient must not move")
+                continue
+            rel = np.linalg.norm(up_mine - up_ref) / np.linalg.norm(up_ref)
+            assert rel < 0.25, (step, i, rel)
+
+
+@pytest.mark.parametrize("batch_ns,fname", [(True, "traj_hybrid_batch.npz"), (False, "traj_hybrid_nobatch.npz")])
+def test_hybrid_trajectory(batch_ns, fname):
+    d = load(fname)
+    params, opt = hybrid_from_golden(d, batch_ns)
     for step in range(4):
         mine_prev = [bits_of(p).ravel() for p in params]
         for i, p in enumerate(params):
             g = d[f"g{step}_{i}"]
             p.grad = None if g.size == 0 else to_bf16(g, DEV).view(p.shape)
         opt.step()
-        for i, p in enumerate(params):
-            st = opt.state[p]
-            assert int(st.get("step", -1)) == int(d[f"step{step}_{i}"]), ("step", step, i)
-            for key in ("momentum_buffer", "ema", "ema_squared"):
-                k = f"{key}{step}_{i}"
-                if k in d:
-                    assert_bits_equal(bits_of(st[key]).ravel(), d[k].ravel(), f"{key} step {step} param {i}")
-            want = d[f"p{step}_{i}"].ravel()
-            got = bits_of(p).ravel()
-            if i >= 6:
-                assert_bits_equal(got, want, f"AdamW param {i} step {step}")
-            else:
-                # The golden run's prepare went through the Triton interpreter, whose
-                # fp32->bf16 cast truncates instead of rounding, so its Newton-Schulz input
-                # differs from the compiled path by up to one bf16 ulp per element; the
-                # quintic iteration amplifies that to a few percent of the update. Gate: the
-                # applied update agrees with the reference's to within 25% in rel. Frobenius
-                # (exact Muon parity is in test_muon_batch_step_matches_oracle_pipeline).
-                prev = d[f"p{step - 1}_{i}"] if step else d[f"init_{i}"]
-                up_mine = bf16_to_f32(got).astype(np.float64) - bf16_to_f32(prev.ravel())
-                up_ref = bf16_to_f32(want).astype(np.float64) - bf16_to_f32(prev.ravel())
-                if not np.any(up_ref):
-                    assert_bits_equal(got, mine_prev[i], f"param {i} without a gradient must not move")
-                    continue
-                rel = np.linalg.norm(up_mine - up_ref) / np.linalg.norm(up_ref)
-                assert rel < 0.25, (step, i, rel)
+        check_hybrid_step(d, step, params, opt, mine_prev)
 
 
 def test_adamw_centralization_trajectory():
