@@ -203,7 +203,7 @@ def run_ours(args, rank, world, local_rank):
     lib = _lib.load()
     hbm_gbs, tf_burst, tf_sus, peak_kind = peaks()
     muon, adam = build_tensors(device)
-    shard = Sharder(reserve_sms=args.reserve_sms) if world > 1 else None
+    shard = Sharder(reserve_sms=args.reserve_sms, transport=args.transport) if world > 1 else None
     opt = TritonMuonSRWithAuxAdam([
         dict(params=muon, use_muon=True, lr=0.02, momentum=0.95, weight_decay=0.01),
         dict(params=adam, use_muon=False, lr=3e-4, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
@@ -462,7 +462,7 @@ def run_ours(args, rank, world, local_rank):
             ref_gpu = {"error": f"{type(exc).__name__}: {exc}"[:400]}
         torch.cuda.empty_cache()
     if world > 1:
-        sharded = sharded_bit_check(device)
+        sharded = sharded_bit_check(device, args.transport)
 
     result = None
     if rank == 0:
@@ -474,6 +474,7 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": "configs[3]: TritonMuonSRWithAuxAdam(batch_ns=True) step, Llama-3-8B shapes",
                        "muon_matrices": len(muon), "adamw_tensors": len(adam), "elements": n_all,
                        "parallelism": f"param-sharded x{world}" if world > 1 else "single GPU",
+                       "weight_exchange": shard.transport if shard is not None else None,
                        "l2": "inputs > L2 (126 MB), no flush"},
             "ns_tflops": ns_tflops, "ns_tflop_per_step": total_flops / 1e12,
             "adamw8bit_hbm_gbs": a8_gbs, "adamw8bit_step_ms": a8_step_ms, "adamw8bit_kernel_ms": a8_kernel_ms,
@@ -509,7 +510,7 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
-def sharded_bit_check(device):
+def sharded_bit_check(device, transport):
     """N > 1: the sharded step writes the single-GPU bits. A small hybrid Muon + AdamW step
     (batch_ns, two steps) and an 8-bit AdamW step run twice from the same weights and
     gradients on every rank -- once sharded over all ranks (``Sharder``), once unsharded on
@@ -536,7 +537,7 @@ def sharded_bit_check(device):
     for make in (hybrid, eight_bit):
         pa = [torch.nn.Parameter(t.to(device)) for t in init]
         pb = [torch.nn.Parameter(t.to(device)) for t in init]
-        oa, ob = make(pa, Sharder()), make(pb, None)
+        oa, ob = make(pa, Sharder(transport=transport)), make(pb, None)
         for gs in grads:
             for p, q, gr in zip(pa, pb, gs):
                 p.grad = gr.clone()
@@ -822,6 +823,11 @@ def run_kernel_case(args):
             m, v = torch.zeros_like(p), torch.zeros_like(p)
             fn = lambda: K.adamw_sr([(p, gr, m, v, 1, 7)], 3e-4, 0.9, 0.95, 1e-10, 0.01)
             work = n * 14 / 1e9
+        elif args.kernel == "centralize":
+            rows = n // 4096  # [rows, 4096]: one mean per row, the row read twice (the second from cache)
+            gm = gr.view(rows, 4096)
+            fn = lambda: K.centralize(gm, 0.5)
+            work = n * 4 / 1e9
         elif args.kernel == "accum":
             acc = torch.empty_like(p).normal_(0, 1e-3, generator=g)
             fn = lambda: K.grad_accum_(acc, gr, 1234)
@@ -845,7 +851,8 @@ def run_kernel_case(args):
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
-    out.update({"ms_per_call": ms, "rate": work / (ms * 1e-3), "unit": unit, "small": bool(args.small)})
+    out.update({"ms_per_call": ms, "rate": work / (ms * 1e-3), "unit": unit, "small": bool(args.small),
+                "noise": args.noise})
     print(json.dumps(out), flush=True)
 
 
@@ -859,14 +866,20 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU path (baseline/_ref) next to the engine")
-    ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply", "accum"],
+    ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply", "accum", "centralize"],
                     help="time one kernel alone (profiling cases) instead of the optimizer step")
     ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
+    ap.add_argument("--noise", choices=["reference", "fast", "none"], default="reference",
+                    help="with --kernel: the stochastic-rounding noise stream")
+    ap.add_argument("--transport", choices=["auto", "multicast", "p2p", "nccl"], default="p2p",
+                    help="N>1: how the sharded step shares the updated weights (Sharder transport)")
     ap.add_argument("--reserve-sms", type=int, default=int(os.environ.get("MSR_RESERVE_SMS", "0")),
                     help="N>1: SMs the GEMMs leave to the concurrent weight broadcasts")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.kernel:
+        from muon_sr_b200 import kernels as K
+        K.set_sr_noise(args.noise)
         run_kernel_case(args)
         return
 

@@ -61,6 +61,28 @@ def _issuing():
     return rec is None or rec.launches
 
 
+# Multicast addresses of the parameters this process updates, registered by a
+# ``sharding.Sharder`` whose weights live in a symmetric allocation bound to an NVLink
+# multicast object: data_ptr -> multicast address. The weight-updating launches (apply, AdamW,
+# 8-bit AdamW) pass it as the entry's ``param_mc``, so the updated weight is stored once and
+# reaches every rank's replica.
+_multicast = {}
+
+
+def register_multicast(mapping) -> None:
+    """Add multicast parameter addresses (``{data_ptr: address}``) to the registry."""
+    _multicast.update(mapping)
+
+
+def unregister_multicast(data_ptrs) -> None:
+    for ptr in data_ptrs:
+        _multicast.pop(ptr, None)
+
+
+def _mc(t):
+    return _multicast.get(t.data_ptr()) if _multicast else None
+
+
 # ---------------------------------------------------------------------------------------
 def philox_fill(n: int, ctr_base: int, key: int, device) -> torch.Tensor:
     """Test hook: Philox words for counters ctr_base .. ctr_base + n - 1 (as int32)."""
@@ -116,6 +138,7 @@ def muon_apply(items, lr: float, weight_decay: float) -> None:
         e.numel = p.numel()
         e.key = triton_key(seed)
         e.scale = float(f32(scale))
+        e.param_mc = _mc(p)
     dev = items[0][0].device
     rec = _recorder()
     if rec is not None:
@@ -140,6 +163,7 @@ def adamw_sr(items, lr: float, beta1: float, beta2: float, eps: float, weight_de
         bc2s = (1.0 - beta2 ** step) ** 0.5
         e.step_size = float(f32(lr / bc1))
         e.bc2_sqrt = float(f32(bc2s))
+        e.param_mc = _mc(p)
     hp = _lib.AdamWHparams(float(f32(beta1)), float(f32(1.0 - beta1)), float(f32(beta2)), float(f32(1.0 - beta2)),
                            float(f32(eps)), float(f32(1.0 - lr * weight_decay)))
     dev = items[0][0].device
@@ -187,6 +211,7 @@ def adamw8bit(items, qmap1, qmap2, lr, beta1, beta2, eps, weight_decay, block_si
         e.coef = float(f32(f32(lr32 * sq_bc2) / bc1))
         e.sqrt_bc2_eps = float(f32(sq_bc2 * eps32))
         e.quantized = 1 if quant else 0
+        e.param_mc = _mc(p)
     hp = _lib.Adam8Hparams(float(f32(beta1)), float(f32(1.0 - beta1)), float(f32(beta2)), float(f32(1.0 - beta2)),
                            float(f32(1.0 - lr * weight_decay)), int(block_size),
                            qtables.data_ptr() if qtables is not None else None)

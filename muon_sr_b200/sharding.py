@@ -72,7 +72,18 @@ class Sharder:
 
     Weight sharing (``transport``):
 
-    * ``"p2p"`` (default on CUDA): every rank maps, once, the device allocations that hold
+    * ``"multicast"`` (chosen by the default ``"auto"`` when every rank's GPU supports NVLink
+      multicast): on the first step every parameter is moved into one symmetric allocation
+      (torch symmetric memory: every rank maps every rank's copy, bound to one NVLink
+      multicast object) and becomes a view of its slot there. The owner's weight-updating
+      kernels (apply, AdamW, 8-bit AdamW) then store each updated weight once through the
+      multicast address and the NVSwitch writes it into every rank's replica: the update and
+      the all-gather are one kernel, with no copies, no extra SMs and one outgoing write per
+      element. Ordering: an interprocess event per rank and a host-only (gloo) barrier at the
+      start of the step (no rank may still read weights an owner is about to overwrite) and at
+      its end (every rank waits for every owner's writes). The parameters' storage changes
+      once (``p.data`` is re-pointed); code that cached the old tensors must re-read them.
+    * ``"p2p"`` (``"auto"`` without multicast): every rank maps, once, the device allocations that hold
       the parameters other ranks own (CUDA IPC) and pulls their updated values with
       copy-engine peer copies over NVLink on COPY_STREAMS_PER_PEER side streams per owner, so
       the transfers use no SMs and run under the Newton-Schulz GEMMs (the process needs
@@ -87,13 +98,15 @@ class Sharder:
     * ``"nccl"``: one NCCL broadcast per parameter from its owner.
     """
 
-    def __init__(self, group=None, reserve_sms: int = 0, transport: str = "p2p"):
+    def __init__(self, group=None, reserve_sms: int = 0, transport: str = "auto"):
         """``reserve_sms``: SMs the Newton-Schulz GEMMs leave free for concurrent NCCL
-        kernels (pair it with NCCL_MAX_NCHANNELS <= reserve_sms); 0 keeps every SM."""
+        kernels (pair it with NCCL_MAX_NCHANNELS <= reserve_sms); 0 keeps every SM.
+        ``transport``: "auto" (multicast if every rank supports it, else p2p), "multicast",
+        "p2p" or "nccl"."""
         if not dist.is_available() or not dist.is_initialized():
             raise RuntimeError("Sharder needs an initialised torch.distributed process group")
-        if transport not in ("p2p", "nccl"):
-            raise ValueError("transport must be 'p2p' or 'nccl'")
+        if transport not in ("auto", "multicast", "p2p", "nccl"):
+            raise ValueError("transport must be 'auto', 'multicast', 'p2p' or 'nccl'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -102,17 +115,18 @@ class Sharder:
             sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
             _lib.load().msr_set_gemm_max_ctas(max(1, sms - int(reserve_sms)))
         self.transport = transport if torch.cuda.is_available() else "nccl"
-        if self.transport == "p2p" and int(os.environ.get("CUDA_DEVICE_MAX_CONNECTIONS", "8")) < 8 * COPY_STREAMS_PER_PEER:
+        if self.transport in ("auto", "p2p") and int(os.environ.get("CUDA_DEVICE_MAX_CONNECTIONS", "8")) < 8 * COPY_STREAMS_PER_PEER:
             warnings.warn("Sharder(transport='p2p') runs several copy streams per peer next to the compute stream; "
                           "set CUDA_DEVICE_MAX_CONNECTIONS=32 before CUDA initialises, or copies waiting on peers "
                           "can delay compute kernels that share their hardware queue", RuntimeWarning)
         # host-only barriers for the p2p ordering (created collectively, same order on all ranks);
         # they only wait for the other ranks to issue their work, so a rank that failed ends
         # the others' wait with an error after HOST_BARRIER_TIMEOUT instead of torch's default
-        self._host = dist.new_group(backend="gloo", timeout=HOST_BARRIER_TIMEOUT) if self.transport == "p2p" else None
+        self._host = dist.new_group(backend="gloo", timeout=HOST_BARRIER_TIMEOUT) if self.transport != "nccl" else None
         self._owner = None  # id(param) -> rank within the group
         self._order = None  # params in a fixed order
         self._p2p = None    # lazily built peer mappings
+        self._mc = None     # lazily built multicast weights
 
     # -- plan -----------------------------------------------------------------------------
     def plan(self, param_groups):
@@ -134,6 +148,10 @@ class Sharder:
         self._order = [p for g in param_groups for p in g["params"]]
         self._index = {id(p): i for i, p in enumerate(self._order)}
         self._p2p = None
+        if self._mc:
+            self._mc.close()
+            self._mc = None
+            self.transport = "auto"
         return owner
 
     def loads(self, param_groups):
@@ -153,6 +171,17 @@ class Sharder:
     def bind(self, optimizer):
         self._ensure(optimizer)
         self._groups = optimizer.param_groups
+        if self.transport in ("auto", "multicast"):
+            if self._mc and self._mc.stale():
+                self._mc.close()
+                self._mc = None  # parameters were replaced: build the shared weights again
+            if self._mc is None:
+                ok = _Multicast.possible(self)
+                if not ok and self.transport == "multicast":
+                    raise RuntimeError("Sharder(transport='multicast'): NVLink multicast is not available on every "
+                                       "rank's GPU")
+                self._mc = _Multicast(self) if ok else False
+                self.transport = "multicast" if ok else "p2p"
         if self.transport == "p2p" and self._p2p and self._p2p.stale():
             self._p2p = None  # some owner's weights moved: every rank maps them again
         if self.transport == "p2p" and self._p2p is None:
@@ -166,6 +195,8 @@ class Sharder:
         """Number of consecutive segments a stack of ``n`` matrices of ``shape`` is shared
         in: about SEGMENT_SECONDS of Newton-Schulz per rank each, at least two matrices per
         rank per segment (so the batched GEMMs stay full), at most 8."""
+        if self.transport == "multicast":
+            return 1  # weights travel as the kernels write them: nothing to share in between
         per_rank = n * _ns_flops(tuple(shape)) / TENSOR_FLOPS / self.world
         return max(1, min(8, n // (2 * self.world), round(per_rank / SEGMENT_SECONDS)))
 
@@ -181,6 +212,8 @@ class Sharder:
         self._shared = set()
         self._pending = []
         self._point = 0
+        if self.transport == "multicast":
+            self._mc.begin()
 
     def share(self, params):
         """Start sharing each of ``params`` that has a gradient from its owner. Every rank
@@ -191,6 +224,8 @@ class Sharder:
         todo = [p for p in params if p.grad is not None and id(p) not in self._shared]
         for p in todo:
             self._shared.add(id(p))
+        if self.transport == "multicast":
+            return  # the owners' kernels already wrote every replica
         if self.transport == "p2p":
             self._p2p.share(todo, self._point)
             self._point += 1
@@ -204,6 +239,9 @@ class Sharder:
         """Share whatever was not shared yet, then make the current stream wait for all of
         this step's transfers."""
         self.share(self._order)
+        if self.transport == "multicast":
+            self._mc.finish()
+            return
         if self.transport == "p2p":
             self._p2p.finish()
             return
@@ -316,6 +354,124 @@ class Sharder:
                     if buf is not t:
                         t.copy_(buf)
                     st[k] = t
+
+
+def _event_set(sh, lib):
+    """One interprocess event of this rank plus the opened events of every peer (collective
+    over the host group). Returns (own event, {peer rank: event}, [handles to destroy])."""
+    from . import _lib
+    ev = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    _lib.check(lib.msr_ipc_event_create(ctypes.byref(ev), h), "msr_ipc_event_create")
+    owned = [ev.value]
+    handles = [None] * sh.world
+    dist.all_gather_object(handles, bytes(h.raw), group=sh._host)
+    peers = {}
+    for r, hh in enumerate(handles):
+        if r == sh.rank:
+            continue
+        pe = ctypes.c_void_p()
+        _lib.check(lib.msr_ipc_event_open(hh, ctypes.byref(pe)), "msr_ipc_event_open")
+        owned.append(pe.value)
+        peers[r] = pe.value
+    return ev.value, peers, owned
+
+
+def _cross_rank_point(sh, lib, events, stream):
+    """Every rank's ``stream`` continues only after every rank's stream reached this point:
+    record this rank's event, a host barrier (all records are enqueued), wait for the peers'."""
+    from . import _lib
+    ev, peers, _ = events
+    _lib.check(lib.msr_event_record(ctypes.c_void_p(ev), ctypes.c_void_p(stream.cuda_stream)), "msr_event_record")
+    dist.barrier(group=sh._host)
+    for e in peers.values():
+        _lib.check(lib.msr_stream_wait_event(ctypes.c_void_p(stream.cuda_stream), ctypes.c_void_p(e)),
+                   "msr_stream_wait_event")
+
+
+class _Multicast:
+    """Weights in one symmetric allocation bound to an NVLink multicast object (the
+    ``multicast`` transport). Slots are 128-byte aligned, so every parameter keeps 16-byte
+    alignment and an odd-length parameter is followed by padding the kernels may write."""
+
+    ALIGN = 64  # elements (bf16): 128-byte slots
+
+    @staticmethod
+    def possible(sh) -> bool:
+        """Collective (host group): every rank's GPU supports NVLink multicast and every
+        parameter is a bf16 CUDA tensor."""
+        ok = 0
+        try:
+            import torch.distributed._symmetric_memory  # noqa: F401
+            from torch._C._autograd import DeviceType
+            from torch._C._distributed_c10d import _SymmetricMemory
+            params = sh._order
+            ok = int(bool(params) and all(p.is_cuda and p.dtype == torch.bfloat16 for p in params)
+                     and _SymmetricMemory.has_multicast_support(DeviceType.CUDA, torch.cuda.current_device()))
+        except Exception:
+            ok = 0
+        flags = [None] * sh.world
+        dist.all_gather_object(flags, ok, group=sh._host)
+        return all(flags)
+
+    def __init__(self, sh):
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        from . import kernels as K
+        self.sh = sh
+        self.lib = _lib.load()
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        slots, off = [], 0
+        for p in sh._order:
+            slots.append((p, off))
+            off += (p.numel() + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+        self.flat = symm.empty(max(off, self.ALIGN), dtype=torch.bfloat16, device=self.device)
+        self.handle = symm.rendezvous(self.flat, sh.group if sh.group is not None else dist.group.WORLD)
+        mc = int(self.handle.multicast_ptr)
+        ok = torch.tensor([1 if mc else 0], dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=sh._host)
+        if not int(ok.item()):
+            raise RuntimeError("NVLink multicast address missing after the symmetric-memory rendezvous")
+        base = self.flat.data_ptr()
+        mapping = {}
+        for p, o in slots:
+            view = self.flat[o:o + p.numel()].view_as(p)
+            view.copy_(p.detach())
+            p.data = view
+            if sh._owner[id(p)] == sh.rank:
+                mapping[base + 2 * o] = mc + 2 * o
+        torch.cuda.current_stream(self.device).synchronize()
+        self.exported = [(p, p.data_ptr()) for p, _ in slots]
+        self.registered = list(mapping)
+        K.register_multicast(mapping)
+        self.start = _event_set(sh, self.lib)
+        self.done = _event_set(sh, self.lib)
+
+    def stale(self) -> bool:
+        """Collective (host group): True on every rank if any rank's parameters no longer are
+        the views of the shared allocation (``p.data`` replaced, a module's
+        ``load_state_dict`` that assigned new tensors ...), so all ranks rebuild together."""
+        moved = any(p.data_ptr() != ptr for p, ptr in self.exported)
+        flag = torch.tensor([1 if moved else 0], dtype=torch.int32)
+        dist.all_reduce(flag, group=self.sh._host)
+        return bool(flag.item())
+
+    def begin(self):
+        # no rank may still read (e.g. a backward pass) weights an owner is about to overwrite
+        _cross_rank_point(self.sh, self.lib, self.start, torch.cuda.current_stream(self.device))
+
+    def finish(self):
+        # every owner's multicast writes (fenced at system scope by the kernels) are done
+        _cross_rank_point(self.sh, self.lib, self.done, torch.cuda.current_stream(self.device))
+
+    def close(self):
+        from . import kernels as K
+        K.unregister_multicast(self.registered)
+        self.registered = []
+        for ev in (self.start, self.done):
+            for e in ev[2]:
+                self.lib.msr_event_destroy(ctypes.c_void_p(e))
+        self.start = self.done = (None, {}, [])
 
 
 class _PeerMaps:

@@ -92,16 +92,26 @@ def _bits(t):
     return t.contiguous().view(-1).view(torch.uint8).numpy()
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, transport):
+    import functools
+
     import torch.distributed as dist
     from muon_sr_b200 import Sharder, sharding
     sharding.SEGMENT_SECONDS = 1e-9  # share the larger stacks in segments even at these sizes
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
-                      CUDA_DEVICE_MAX_CONNECTIONS="32")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), CUDA_DEVICE_MAX_CONNECTIONS="32")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        out = _run(torch.device("cuda", rank), Sharder, rank=rank)
+        if transport == "multicast":
+            probe = Sharder(transport="auto")
+            probe._order = [torch.zeros(8, dtype=torch.bfloat16, device="cuda")]
+            if not sharding._Multicast.possible(probe):
+                if rank == 0:
+                    q.put("no multicast")
+                dist.barrier()
+                return
+        out = _run(torch.device("cuda", rank), functools.partial(Sharder, transport=transport), rank=rank)
+        torch.cuda.synchronize()
         if rank == 0:
             q.put([_bits(t) for t in out])
         dist.barrier()
@@ -110,18 +120,23 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_sharded_step_equals_single_gpu():
+@pytest.mark.parametrize("transport", ["p2p", "multicast"])
+def test_two_gpu_sharded_step_equals_single_gpu(transport):
+    """Weights shared by copy-engine peer pulls (p2p) or stored by the owners' kernels through
+    an NVLink multicast address (multicast): the same bits as one GPU."""
     import numpy as np
     single = [_bits(t) for t in _run(torch.device("cuda", 0), None)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + os.getpid() % 500
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29700 + os.getpid() % 500 + (7 if transport == "multicast" else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     sharded = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    if sharded == "no multicast":
+        pytest.skip("NVLink multicast is not available on these GPUs")
     for i, (a, b) in enumerate(zip(single, sharded)):
         assert np.array_equal(a, b), f"tensor {i} (parameters, then optimizer state) differs between 1 and 2 GPUs"
