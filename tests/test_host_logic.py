@@ -244,8 +244,11 @@ def test_sharder_segment_counts():
     """About 4 ms of per-rank Newton-Schulz per segment, at least two matrices per rank per
     segment, at most 8 segments; small stacks stay whole."""
     class Fake(Sharder):
-        def __init__(self, world):  # no process group needed for the arithmetic
+        def __init__(self, world, transport="p2p"):  # no process group needed for the arithmetic
             self.world = world
+            self.transport = transport
+    # the multicast transport has nothing to share between segments: whole stacks
+    assert all(Fake(8, "multicast").segments(shape, 64) == 1 for shape in ((4096, 4096), (14336, 4096)))
     expect = {2: {(4096, 4096): 8, (1024, 4096): 1, (14336, 4096): 8, (4096, 14336): 8},
               8: {(4096, 4096): 2, (1024, 4096): 1, (14336, 4096): 4, (4096, 14336): 2}}
     counts = {(4096, 4096): 64, (1024, 4096): 64, (14336, 4096): 64, (4096, 14336): 32}
