@@ -801,6 +801,8 @@ def run_kernel_case(args):
     out = {"kernel": args.kernel}
     if args.kernel == "ns":
         shape = (4, D, D) if args.small else (16, D, D)
+        if args.ns_shape:
+            shape = tuple(int(v) for v in args.ns_shape.split("x"))
         x = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(0, 1e-3, generator=g)
         fn = lambda: K.newton_schulz(x, 5)
         work = shape[0] * ns_flops(shape[1:]) / 1e12
@@ -869,6 +871,8 @@ def main():
     ap.add_argument("--kernel", choices=["ns", "adamw8bit", "adamw", "prepare", "apply", "accum", "centralize"],
                     help="time one kernel alone (profiling cases) instead of the optimizer step")
     ap.add_argument("--small", action="store_true", help="with --kernel: the few-GB profiling size")
+    ap.add_argument("--ns-shape", default=None,
+                    help="with --kernel ns: the stack as BATCHxROWSxCOLS (e.g. 12x768x3072)")
     ap.add_argument("--noise", choices=["reference", "fast", "none"], default="reference",
                     help="with --kernel: the stochastic-rounding noise stream")
     ap.add_argument("--transport", choices=["auto", "multicast", "p2p", "nccl"], default="p2p",
