@@ -17,7 +17,7 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 SHAPES_MUON = [(256, 512)] * 9 + [(512, 256)] * 2 + [(128, 384)] * 2
-SHAPES_ADAM = [(1000, 64), (64,), (64,)]
+SHAPES_ADAM = [(1000, 64), (64,), (64,), (67,)]  # 67: a ragged end (4-byte multicast pairs)
 
 
 def _params(device):
