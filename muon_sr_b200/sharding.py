@@ -22,6 +22,7 @@ NVLink / NVSwitch, so the step's work is divided by the number of ranks.
 import ctypes
 import datetime
 import heapq
+import math
 import os
 import warnings
 
@@ -319,8 +320,11 @@ class Sharder:
         """Collective: copy every parameter's optimizer state from its owner to rank ``dst``
         (every rank when None), so that ``optimizer.state_dict()`` there holds the whole
         state with the reference's keys and dtypes (checkpoints stay interchangeable with
-        the single-GPU classes). Loading needs no counterpart: every rank loads the full
-        checkpoint and uses the part it owns."""
+        the single-GPU classes). Each owner packs all the state tensors it holds into one
+        byte buffer (16-byte aligned slots, any dtype), so the transfer is one broadcast per
+        owner (``dst`` None) or one send/receive pair per owner (``dst`` given; ranks other
+        than the owner and ``dst`` move nothing) -- not one collective per tensor. Loading
+        needs no counterpart: every rank loads the full checkpoint and uses the part it owns."""
         self._ensure(optimizer)
         order = [p for g in optimizer.param_groups for p in g["params"]]
         meta = {}
@@ -331,29 +335,47 @@ class Sharder:
                        for k, v in optimizer.state.get(p, {}).items()}
         metas = [None] * self.world
         dist.all_gather_object(metas, meta, group=self.group)
-        for i, p in enumerate(order):
-            owner = self._owner[id(p)]
-            spec = metas[owner].get(i)
-            if not spec:
+        device = order[0].device if order else torch.device("cpu")
+        for owner in range(self.world):
+            receive = owner != self.rank and (dst is None or dst == self.rank)
+            items, size = [], 0
+            for i in sorted(metas[owner]):
+                p = order[i]
+                for k, spec in sorted(metas[owner][i].items()):
+                    if spec[0] == "v":
+                        if receive:
+                            optimizer.state[p][k] = spec[1]
+                        continue
+                    shape, dtype = spec[1], getattr(torch, spec[2])
+                    nbytes = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+                    items.append((p, k, shape, dtype, size, nbytes))
+                    size = (size + nbytes + 15) // 16 * 16
+            if size == 0 or (dst is not None and owner == dst):
                 continue
-            keep = owner != self.rank and (dst is None or dst == self.rank)
-            st = optimizer.state[p]
-            for k in sorted(spec):
-                kind = spec[k][0]
-                if kind == "v":
-                    if keep:
-                        st[k] = spec[k][1]
-                    continue
-                shape, dtype = spec[k][1], getattr(torch, spec[k][2])
-                t = st.get(k) if torch.is_tensor(st.get(k)) else None
-                if owner != self.rank and (t is None or tuple(t.shape) != shape or t.dtype != dtype):
-                    t = torch.empty(shape, dtype=dtype, device=p.device)
-                buf = t if t.is_contiguous() else t.contiguous()
+            if self.rank == owner:
+                buf = torch.empty(size, dtype=torch.uint8, device=device)
+                for p, k, shape, dtype, off, nbytes in items:
+                    buf[off:off + nbytes].copy_(optimizer.state[p][k].contiguous().view(-1).view(torch.uint8))
+            elif dst is None or dst == self.rank:
+                buf = torch.empty(size, dtype=torch.uint8, device=device)
+            else:
+                continue  # a point-to-point transfer between the owner and dst
+            if dst is None:
                 dist.broadcast(buf, src=self._src(owner), group=self.group)
-                if keep:
-                    if buf is not t:
-                        t.copy_(buf)
-                    st[k] = t
+            elif self.rank == owner:
+                dist.send(buf, dst=self._src(dst), group=self.group)
+            else:
+                dist.recv(buf, src=self._src(owner), group=self.group)
+            if not receive:
+                continue
+            for p, k, shape, dtype, off, nbytes in items:
+                st = optimizer.state[p]
+                t = st.get(k)
+                if not (torch.is_tensor(t) and tuple(t.shape) == shape and t.dtype == dtype and t.is_contiguous()
+                        and t.device == buf.device):
+                    t = torch.empty(shape, dtype=dtype, device=buf.device)
+                t.view(-1).view(torch.uint8).copy_(buf[off:off + nbytes])
+                st[k] = t
 
 
 def _event_set(sh, lib):
