@@ -2,21 +2,17 @@
 // prepare (momentum + Nesterov), Muon apply (decay + scaled update) and AdamW-SR.
 //
 // Design (B200): multi-tensor launches. Each launch carries up to MAXE tensors in its
-// kernel parameters; the work is cut into tiles of 2048 elements that never cross a tensor,
-// and a persistent grid (a multiple of the SM count) walks the tiles. Inside each CTA a
-// producer warp streams the tiles' inputs into a shared-memory ring with bulk asynchronous
-// copies while eight consumer warps compute (stream.cuh): the kernels are bound by the
-// FMA-heavy pipe that runs the reference's Philox multiplies, and the ring keeps HBM busy
-// underneath that work. Each consumer thread handles 8 bf16 per tile with 16-byte shared
-// loads and 16-byte global stores. All fp32 arithmetic uses explicit round-to-nearest
-// intrinsics (no contraction into FMA), in the reference's op order, so results are
-// bit-identical to the reference kernels' fp32 evaluation. Every kernel is instantiated per
-// noise mode (msr_set_sr_noise), and prepare / apply / AdamW once more (REC) for the
-// replayable launches that read their scalars and entries from a device record (msr_*_rec,
-// used inside captured CUDA graphs).
+// kernel parameters; the work is cut into chunks of 8192 elements that never cross a
+// tensor, and a persistent grid (a multiple of the SM count) walks the chunks. Each thread
+// moves 8 bf16 per 16-byte access, issuing all loads of a chunk before its math so that
+// every SM keeps enough bytes in flight for HBM3e. All fp32 arithmetic uses explicit
+// round-to-nearest intrinsics (no contraction into FMA), in the reference's op order, so
+// results are bit-identical to the reference kernels' fp32 evaluation. Every kernel is
+// instantiated per noise mode (msr_set_sr_noise), and prepare / apply / AdamW once more
+// (REC) for the replayable launches that read their scalars and entries from a device
+// record (msr_*_rec, used inside captured CUDA graphs).
 #include "common.cuh"
 #include "host_common.h"
-#include "stream.cuh"
 
 #include <algorithm>
 
@@ -26,15 +22,15 @@ namespace {
 constexpr int EW_THREADS = 256;
 constexpr int EW_VEC = 8;
 constexpr int EW_ITERS = 2;
-constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 8192 elements (first-micro-batch copy)
+constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 8192 elements
 constexpr int MAXE = 64;
 constexpr int EW_BLOCKS_PER_SM = 4;
-constexpr int64_t TILE = stream::TILE;
-// Streamed kernels: ring stages and CTAs per SM. Prepare, apply and SR accumulation stream
-// two bf16 arrays (8 KB per stage); AdamW streams four (16 KB per stage) and keeps three
-// Philox chains per element, so it runs two CTAs per SM with more registers each.
-constexpr int EW_STAGES = 4, EW_MINB = 3;
-constexpr int ADAMW_STAGES = 4, ADAMW_MINB = 2;
+// AdamW: 2 vectors of 8 per thread and chunk at 2 CTAs per SM measured faster (1425 GB/s on
+// 2^28 elements) than 1 vector at 4 CTAs per SM (1368 GB/s), where the three Philox chains per
+// element no longer fit the 64-register budget.
+constexpr int ADAMW_ITERS = 2;
+constexpr int ADAMW_MINB = 2;
+constexpr int64_t ADAMW_CHUNK = EW_THREADS * EW_VEC * ADAMW_ITERS;
 
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
@@ -46,24 +42,6 @@ __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b)
 __global__ void philox_fill_kernel(uint32_t* out, int64_t n, uint64_t ctr_base, PhiloxKey key) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = philox_word0(static_cast<uint32_t>(ctr_base + static_cast<uint64_t>(i)), key);
-}
-
-// 8 bf16 from shared memory (16 bytes).
-__device__ __forceinline__ U16x8 lds_u16x8(const uint16_t* p) {
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "r"(tc::smem_addr(p)));
-  U16x8 o;
-  *reinterpret_cast<uint4*>(o.v) = r;
-  return o;
-}
-
-// Dynamic shared memory of a streamed kernel (the ring of stream::Smem).
-template <int NIN, int S>
-__device__ __forceinline__ stream::Smem<NIN, S>& ring() {
-  extern __shared__ __align__(128) uint8_t dsm[];
-  return *reinterpret_cast<stream::Smem<NIN, S>*>(dsm);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -93,48 +71,48 @@ __global__ __launch_bounds__(EW_THREADS) void grad_accum_first_kernel(uint16_t* 
     acc[i] = first_one(g[i]);
 }
 
-// One tensor per launch (the accumulator hook runs per parameter).
-struct AccumArgs {
-  uint16_t* acc;
-  const uint16_t* g;
-  int64_t n;
-  int64_t prefix[2];
-  PhiloxKey key;
-  int vec;
-};
-
-template <int NOISE>
-struct AccumPolicy {
-  static constexpr int NIN = 2;  // acc, g
-  const AccumArgs& a;
-  __device__ int count() const { return 1; }
-  __device__ const int64_t* prefix() const { return a.prefix; }
-  __device__ bool vec(int) const { return a.vec != 0; }
-  __device__ int64_t numel(int) const { return a.n; }
-  __device__ const void* input(int, int i) const { return i == 0 ? static_cast<const void*>(a.acc) : a.g; }
-  __device__ void vector8(int, int64_t idx, const uint16_t* const (&in)[2]) const {
-    constexpr bool FAST = NOISE == NOISE_FAST;
-    const SrNoise<NOISE> nz{a.key};
-    const U16x8 va = lds_u16x8(in[0]), vg = lds_u16x8(in[1]);
-    uint32_t r[EW_VEC];
-    if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
-    U16x8 o;
+template <bool VEC, int NOISE>
+__global__ __launch_bounds__(EW_THREADS, 4) void grad_accum_kernel(uint16_t* __restrict__ acc,
+                                                               const uint16_t* __restrict__ g,
+                                                               int64_t n, PhiloxKey key) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
+  const SrNoise<NOISE> nz{key};
+  const int64_t nchunks = (n + EW_CHUNK - 1) / EW_CHUNK;
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const int64_t base = chunk * EW_CHUNK;
+    if (VEC) {
+      U16x8 va[EW_ITERS], vg[EW_ITERS];
 #pragma unroll
-    for (int j = 0; j < EW_VEC; ++j)
-      o.v[j] = accum_one<NOISE>(va.v[j], vg.v[j], FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
-    st_u16x8(a.acc + idx, o);
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          va[it] = ld_u16x8(acc + idx);
+          vg[it] = ld_u16x8_stream(g + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 o;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            o.v[j] = accum_one<NOISE>(va[it].v[j], vg[it].v[j],
+                                      FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
+          st_u16x8(acc + idx, o);
+        } else {
+          for (int64_t i = idx; i < n; ++i) acc[i] = accum_one<NOISE>(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) acc[i] = accum_one<NOISE>(acc[i], g[i], nz.at(static_cast<uint64_t>(i)));
+      }
+    }
   }
-  __device__ void scalar_range(int, int64_t lo, int64_t hi) const {
-    const SrNoise<NOISE> nz{a.key};
-    for (int64_t i = lo; i < hi; ++i) a.acc[i] = accum_one<NOISE>(a.acc[i], a.g[i], nz.at(static_cast<uint64_t>(i)));
-  }
-  __device__ bool multicast() const { return false; }
-};
-
-template <int NOISE>
-__global__ __launch_bounds__(stream::THREADS, EW_MINB) void grad_accum_kernel(const __grid_constant__ AccumArgs a,
-                                                                           int* err) {
-  stream::run(AccumPolicy<NOISE>{a}, ring<2, EW_STAGES>(), err);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -178,57 +156,65 @@ __device__ __forceinline__ void prepare_one(uint16_t g_bits, uint16_t b_bits, fl
 }
 
 template <int NOISE, bool REC>
-struct PreparePolicy {
-  static constexpr int NIN = 2;  // grad, momentum
-  const PrepareArgs& a;
-  __device__ int count() const { return a.count; }
-  __device__ const int64_t* prefix() const { return a.prefix; }
-  __device__ bool vec(int e) const { return a.vec[e] != 0; }
-  __device__ int64_t numel(int e) const { return entry_of<REC>(a, e).numel; }
-  __device__ const void* input(int e, int i) const {
-    const msr_prepare_entry& E = entry_of<REC>(a, e);
-    return i == 0 ? E.grad : static_cast<const void*>(E.momentum);
-  }
-  __device__ void vector8(int e, int64_t idx, const uint16_t* const (&in)[2]) const {
-    constexpr bool FAST = NOISE == NOISE_FAST;
-    const msr_prepare_entry& E = entry_of<REC>(a, e);
-    const SrNoise<NOISE> nz{make_key(E.key)};
-    const uint64_t c0 = E.ctr_base + static_cast<uint64_t>(idx);
-    const bool nesterov = (REC ? a.rec->nesterov : a.nesterov) != 0;
-    const float beta = beta_of<REC>(a), omb = omb_of<REC>(a);
-    const U16x8 vg = lds_u16x8(in[0]), vb = lds_u16x8(in[1]);
-    uint32_t r[EW_VEC];
-    if (FAST) nz.eight(c0, r);
-    U16x8 ob, ou;
-#pragma unroll
-    for (int j = 0; j < EW_VEC; ++j)
-      prepare_one<NOISE>(vg.v[j], vb.v[j], beta, omb, nesterov, [&] { return FAST ? r[j] : nz.at(c0 + j); }, ob.v[j],
-                         ou.v[j]);
-    st_u16x8(static_cast<uint16_t*>(E.momentum) + idx, ob);
-    st_u16x8(static_cast<uint16_t*>(E.update) + idx, ou);
-  }
-  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
-    const msr_prepare_entry& E = entry_of<REC>(a, e);
-    const SrNoise<NOISE> nz{make_key(E.key)};
+__global__ __launch_bounds__(EW_THREADS, 4) void muon_prepare_kernel(const __grid_constant__ PrepareArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
+  const int64_t total = a.prefix[a.count];
+  const bool nesterov = (REC ? a.rec->nesterov : a.nesterov) != 0;
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_prepare_entry& E = entry_of<REC>(a, ei);
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* mb = static_cast<uint16_t*>(E.momentum);
     uint16_t* up = static_cast<uint16_t*>(E.update);
-    const bool nesterov = (REC ? a.rec->nesterov : a.nesterov) != 0;
-    for (int64_t i = lo; i < hi; ++i) {
-      uint16_t ob, ou;
-      prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov,
-                         [&] { return nz.at(E.ctr_base + static_cast<uint64_t>(i)); }, ob, ou);
-      mb[i] = ob;
-      up[i] = ou;
+    const int64_t n = E.numel;
+    const SrNoise<NOISE> nz{make_key(E.key)};
+    const uint64_t cb = E.ctr_base;
+    const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
+    if (a.vec[ei]) {
+      U16x8 vg[EW_ITERS], vb[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vg[it] = ld_u16x8_stream(g + idx);
+          vb[it] = ld_u16x8(mb + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 ob, ou;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(cb + static_cast<uint64_t>(idx), r);
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            prepare_one<NOISE>(vg[it].v[j], vb[it].v[j], beta_of<REC>(a), omb_of<REC>(a), nesterov,
+                               [&] { return FAST ? r[j] : nz.at(cb + static_cast<uint64_t>(idx + j)); }, ob.v[j],
+                               ou.v[j]);
+          st_u16x8(mb + idx, ob);
+          st_u16x8(up + idx, ou);
+        } else {
+          for (int64_t i = idx; i < n; ++i) {
+            uint16_t ob, ou;
+            prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+            mb[i] = ob;
+            up[i] = ou;
+          }
+        }
+      }
+    } else {
+      for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) {
+          uint16_t ob, ou;
+          prepare_one<NOISE>(g[i], mb[i], beta_of<REC>(a), omb_of<REC>(a), nesterov, [&] { return nz.at(cb + static_cast<uint64_t>(i)); }, ob, ou);
+          mb[i] = ob;
+          up[i] = ou;
+        }
+      }
     }
   }
-  __device__ bool multicast() const { return false; }
-};
-
-template <int NOISE, bool REC>
-__global__ __launch_bounds__(stream::THREADS, EW_MINB) void muon_prepare_kernel(
-    const __grid_constant__ PrepareArgs a, int* err) {
-  stream::run(PreparePolicy<NOISE, REC>{a}, ring<2, EW_STAGES>(), err);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -242,7 +228,7 @@ struct ApplyArgs {
   float lr, decay;
   const msr_apply_record* rec;  // msr_muon_apply_rec (see PrepareArgs)
   int32_t src[MAXE];
-  int any_mc;  // some entry stores through a multicast address
+  int any_mc;  // some entry stores its weights through a multicast address
 };
 
 template <bool REC>
@@ -264,63 +250,81 @@ __device__ __forceinline__ uint16_t apply_one(uint16_t p_bits, uint16_t u_bits, 
   return round_bf16<NOISE>(p, rnd);
 }
 
+// Elements lo .. hi - 1 of one apply entry, one thread: plain stores, or (multicast weights)
+// 4-byte pairs from an even index -- a pair past the last element writes 0 into the padding
+// that follows the parameter's slot.
 template <int NOISE, bool REC>
-struct ApplyPolicy {
-  static constexpr int NIN = 2;  // param, update
-  const ApplyArgs& a;
-  __device__ int count() const { return a.count; }
-  __device__ const int64_t* prefix() const { return a.prefix; }
-  __device__ bool vec(int e) const { return a.vec[e] != 0; }
-  __device__ int64_t numel(int e) const { return entry_of<REC>(a, e).numel; }
-  __device__ const void* input(int e, int i) const {
-    const msr_apply_entry& E = entry_of<REC>(a, e);
-    return i == 0 ? static_cast<const void*>(E.param) : E.update;
+__device__ __forceinline__ void apply_tail(const ApplyArgs& a, uint16_t* p, uint16_t* pm, const uint16_t* u,
+                                           float scale, const SrNoise<NOISE>& nz, int64_t lo, int64_t hi) {
+  auto one = [&](int64_t i) {
+    return apply_one<NOISE>(p[i], u[i], scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
+  };
+  if (!pm) {
+    for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
+    return;
   }
-  __device__ void vector8(int e, int64_t idx, const uint16_t* const (&in)[2]) const {
-    constexpr bool FAST = NOISE == NOISE_FAST;
-    const msr_apply_entry& E = entry_of<REC>(a, e);
-    const SrNoise<NOISE> nz{make_key(E.key)};
-    const float scale = E.scale, lr = lr_of<REC>(a), decay = decay_of<REC>(a);
-    const U16x8 vp = lds_u16x8(in[0]), vu = lds_u16x8(in[1]);
-    uint32_t r[EW_VEC];
-    if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
-    U16x8 o;
-#pragma unroll
-    for (int j = 0; j < EW_VEC; ++j)
-      o.v[j] = apply_one<NOISE>(vp.v[j], vu.v[j], scale, lr, decay,
-                                FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
-    if (E.param_mc)
-      mc_st_u16x8(static_cast<uint16_t*>(E.param_mc) + idx, o);
-    else
-      st_u16x8(static_cast<uint16_t*>(E.param) + idx, o);
+  for (int64_t i = lo; i < hi; i += 2) {
+    const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
+    mc_st_u32(pm + i, v0 | (v1 << 16));
   }
-  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
-    const msr_apply_entry& E = entry_of<REC>(a, e);
-    const SrNoise<NOISE> nz{make_key(E.key)};
-    uint16_t* p = static_cast<uint16_t*>(E.param);
-    const uint16_t* u = static_cast<const uint16_t*>(E.update);
-    auto one = [&](int64_t i) {
-      return apply_one<NOISE>(p[i], u[i], E.scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
-    };
-    if (!E.param_mc) {
-      for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
-      return;
-    }
-    // multicast: 4-byte pairs from an even index (lo is a multiple of 8); a pair past the
-    // last element writes 0 into the slot's padding
-    uint16_t* mc = static_cast<uint16_t*>(E.param_mc);
-    for (int64_t i = lo; i < hi; i += 2) {
-      const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
-      mc_st_u32(mc + i, v0 | (v1 << 16));
-    }
-  }
-  __device__ bool multicast() const { return a.any_mc != 0; }
-};
+}
 
 template <int NOISE, bool REC>
-__global__ __launch_bounds__(stream::THREADS, EW_MINB) void muon_apply_kernel(const __grid_constant__ ApplyArgs a,
-                                                                           int* err) {
-  stream::run(ApplyPolicy<NOISE, REC>{a}, ring<2, EW_STAGES>(), err);
+__global__ __launch_bounds__(EW_THREADS, 4) void muon_apply_kernel(const __grid_constant__ ApplyArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
+  const int64_t total = a.prefix[a.count];
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_apply_entry& E = entry_of<REC>(a, ei);
+    uint16_t* p = static_cast<uint16_t*>(E.param);
+    uint16_t* pm = static_cast<uint16_t*>(E.param_mc);  // multicast weights (sharded steps)
+    const uint16_t* u = static_cast<const uint16_t*>(E.update);
+    const int64_t n = E.numel;
+    const SrNoise<NOISE> nz{make_key(E.key)};
+    const float scale = E.scale;
+    const int64_t base = (chunk - a.prefix[ei]) * EW_CHUNK;
+    if (a.vec[ei]) {
+      U16x8 vp[EW_ITERS], vu[EW_ITERS];
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vp[it] = ld_u16x8(p + idx);
+          vu[it] = ld_u16x8_stream(u + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < EW_ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          U16x8 o;
+          uint32_t r[EW_VEC];
+          if (FAST) nz.eight(static_cast<uint64_t>(idx), r);
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j)
+            o.v[j] = apply_one<NOISE>(vp[it].v[j], vu[it].v[j], scale, lr_of<REC>(a), decay_of<REC>(a),
+                                      FAST ? r[j] : nz.at(static_cast<uint64_t>(idx + j)));
+          if (pm)
+            mc_st_u16x8(pm + idx, o);
+          else
+            st_u16x8(p + idx, o);
+        } else {
+          apply_tail<NOISE, REC>(a, p, pm, u, scale, nz, idx, n);
+        }
+      }
+    } else {
+      if (pm) {  // an unaligned entry with multicast weights: 4-byte pairs, thread-contiguous
+        const int64_t lo = base + static_cast<int64_t>(threadIdx.x) * (EW_ITERS * EW_VEC);
+        apply_tail<NOISE, REC>(a, p, pm, u, scale, nz, lo, lo + EW_ITERS * EW_VEC < n ? lo + EW_ITERS * EW_VEC : n);
+      } else {
+        for (int it = 0; it < EW_ITERS * EW_VEC; ++it) {
+          const int64_t i = base + it * EW_THREADS + threadIdx.x;
+          if (i < n) p[i] = apply_one<NOISE>(p[i], u[i], scale, lr_of<REC>(a), decay_of<REC>(a), nz.at(static_cast<uint64_t>(i)));
+        }
+      }
+    }
+  }
+  if (a.any_mc) __threadfence_system();  // multicast stores ordered before the callers' barrier
 }
 
 // ---------------------------------------------------------------------------------------
@@ -334,7 +338,7 @@ struct AdamWArgs {
   msr_adamw_hparams hp;
   const msr_adamw_record* rec;  // msr_adamw_sr_rec (see PrepareArgs)
   int32_t src[MAXE];
-  int any_mc;  // some entry stores through a multicast address
+  int any_mc;  // some entry stores its weights through a multicast address
 };
 
 template <bool REC>
@@ -365,92 +369,112 @@ __device__ __forceinline__ void adamw_one(uint16_t& p_bits, uint16_t g_bits, uin
   p_bits = round_bf16<NOISE>(p, rnd(2));
 }
 
+// Elements lo .. hi - 1 of one AdamW entry, one thread: plain stores, or (multicast weights)
+// the weights in 4-byte pairs from an even index (a pair past the last element writes 0 into
+// the padding that follows the parameter's slot); the moments are always local.
 template <int NOISE, bool REC>
-struct AdamWPolicy {
-  static constexpr int NIN = 4;  // param, grad, exp_avg, exp_avg_sq
-  const AdamWArgs& a;
-  __device__ int count() const { return a.count; }
-  __device__ const int64_t* prefix() const { return a.prefix; }
-  __device__ bool vec(int e) const { return a.vec[e] != 0; }
-  __device__ int64_t numel(int e) const { return entry_of<REC>(a, e).numel; }
-  __device__ const void* input(int e, int i) const {
-    const msr_adamw_entry& E = entry_of<REC>(a, e);
-    return i == 0 ? static_cast<const void*>(E.param) : i == 1 ? E.grad : i == 2 ? E.exp_avg : E.exp_avg_sq;
+__device__ __forceinline__ void adamw_tail(const AdamWArgs& a, const msr_adamw_entry& E, const SrNoise<NOISE>& nm,
+                                           const SrNoise<NOISE>& nv, const SrNoise<NOISE>& np_, int64_t lo,
+                                           int64_t hi) {
+  uint16_t* p = static_cast<uint16_t*>(E.param);
+  uint16_t* pm = static_cast<uint16_t*>(E.param_mc);
+  const uint16_t* g = static_cast<const uint16_t*>(E.grad);
+  uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
+  uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
+  auto one = [&](int64_t i) {
+    uint16_t pb = p[i], mb = m[i], vb = v[i];
+    const uint64_t c = static_cast<uint64_t>(i);
+    adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), E.step_size, E.bc2_sqrt,
+                     [&](int w) { return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c); });
+    m[i] = mb;
+    v[i] = vb;
+    return pb;
+  };
+  if (!pm) {
+    for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
+    return;
   }
-  __device__ void vector8(int e, int64_t idx, const uint16_t* const (&in)[4]) const {
-    constexpr bool FAST = NOISE == NOISE_FAST;
-    const msr_adamw_entry& E = entry_of<REC>(a, e);
-    SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
-    const float ss = E.step_size, bc2s = E.bc2_sqrt;
-    const msr_adamw_hparams& hp = hp_of<REC>(a);
-    U16x8 vp = lds_u16x8(in[0]), vm = lds_u16x8(in[2]), vv = lds_u16x8(in[3]);
-    const U16x8 vg = lds_u16x8(in[1]);
-    if constexpr (FAST) {
-      uint32_t rm[EW_VEC], rv[EW_VEC], rp[EW_VEC];
-      nm.eight(static_cast<uint64_t>(idx), rm);
-      nv.eight(static_cast<uint64_t>(idx), rv);
-      np_.eight(static_cast<uint64_t>(idx), rp);
-#pragma unroll
-      for (int j = 0; j < EW_VEC; ++j)
-        adamw_one<NOISE>(vp.v[j], vg.v[j], vm.v[j], vv.v[j], hp, ss, bc2s,
-                         [&](int w) { return w == 0 ? rm[j] : w == 1 ? rv[j] : rp[j]; });
-    } else {
-      // One Philox word per stream and element (m, v, p: three independent chains). The
-      // elements run one after another: an empty asm takes each element's outputs and
-      // "rewrites" the counter base the next element's chains start from, so the compiler
-      // cannot interleave all 24 chains of the vector (which spills); three chains per
-      // thread and two CTAs per SM still keep the FMA-heavy pipe fed.
-      uint32_t cb = static_cast<uint32_t>(idx);
-#pragma unroll
-      for (int j = 0; j < EW_VEC; ++j) {
-        const uint32_t c = cb + static_cast<uint32_t>(j);
-        adamw_one<NOISE>(vp.v[j], vg.v[j], vm.v[j], vv.v[j], hp, ss, bc2s,
-                         [&](int w) { return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c); });
-        const uint32_t om = vm.v[j], ov = vv.v[j], op = vp.v[j];
-        asm volatile("" : "+r"(cb), "+r"(nm.key.k0), "+r"(nm.key.k1), "+r"(nv.key.k0), "+r"(nv.key.k1),
-                     "+r"(np_.key.k0), "+r"(np_.key.k1) : "r"(om), "r"(ov), "r"(op));
-      }
-    }
-    if (E.param_mc)
-      mc_st_u16x8(static_cast<uint16_t*>(E.param_mc) + idx, vp);
-    else
-      st_u16x8(static_cast<uint16_t*>(E.param) + idx, vp);
-    st_u16x8(static_cast<uint16_t*>(E.exp_avg) + idx, vm);
-    st_u16x8(static_cast<uint16_t*>(E.exp_avg_sq) + idx, vv);
+  for (int64_t i = lo; i < hi; i += 2) {
+    const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
+    mc_st_u32(pm + i, v0 | (v1 << 16));
   }
-  __device__ void scalar_range(int e, int64_t lo, int64_t hi) const {
-    const msr_adamw_entry& E = entry_of<REC>(a, e);
-    const SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
+}
+
+// ITERS vectors of 8 elements per thread and chunk; MINB CTAs per SM for the register budget.
+template <int ITERS, int MINB, int NOISE, bool REC>
+__global__ __launch_bounds__(EW_THREADS, MINB) void adamw_kernel(const __grid_constant__ AdamWArgs a) {
+  constexpr bool FAST = NOISE == NOISE_FAST;
+  constexpr int64_t CHUNK = EW_THREADS * EW_VEC * ITERS;
+  const int64_t total = a.prefix[a.count];
+  for (int64_t chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    const int ei = find_entry<MAXE>(a.prefix, a.count, chunk);
+    const msr_adamw_entry& E = entry_of<REC>(a, ei);
     uint16_t* p = static_cast<uint16_t*>(E.param);
+    uint16_t* pm = static_cast<uint16_t*>(E.param_mc);  // multicast weights (sharded steps)
     const uint16_t* g = static_cast<const uint16_t*>(E.grad);
     uint16_t* m = static_cast<uint16_t*>(E.exp_avg);
     uint16_t* v = static_cast<uint16_t*>(E.exp_avg_sq);
-    auto one = [&](int64_t i) {
-      uint16_t pb = p[i], mb = m[i], vb = v[i];
-      const uint64_t c = static_cast<uint64_t>(i);
-      adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), E.step_size, E.bc2_sqrt,
-                       [&](int w) { return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c); });
-      m[i] = mb;
-      v[i] = vb;
-      return pb;
-    };
-    if (!E.param_mc) {
-      for (int64_t i = lo; i < hi; ++i) p[i] = one(i);
-      return;
-    }
-    uint16_t* mc = static_cast<uint16_t*>(E.param_mc);  // pairs, as in ApplyPolicy
-    for (int64_t i = lo; i < hi; i += 2) {
-      const uint32_t v0 = one(i), v1 = i + 1 < hi ? one(i + 1) : 0u;
-      mc_st_u32(mc + i, v0 | (v1 << 16));
+    const int64_t n = E.numel;
+    const SrNoise<NOISE> nm{make_key(E.key_m)}, nv{make_key(E.key_v)}, np_{make_key(E.key_p)};
+    const float ss = E.step_size, bc2s = E.bc2_sqrt;
+    const int64_t base = (chunk - a.prefix[ei]) * CHUNK;
+    if (a.vec[ei]) {
+      U16x8 vp[ITERS], vg[ITERS], vm[ITERS], vv[ITERS];
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          vp[it] = ld_u16x8(p + idx);
+          vg[it] = ld_u16x8_stream(g + idx);
+          vm[it] = ld_u16x8(m + idx);
+          vv[it] = ld_u16x8(v + idx);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const int64_t idx = base + (int64_t)(it * EW_THREADS + threadIdx.x) * EW_VEC;
+        if (idx + EW_VEC <= n) {
+          uint32_t rm[EW_VEC], rv[EW_VEC], rp[EW_VEC];
+          if (FAST) {
+            nm.eight(static_cast<uint64_t>(idx), rm);
+            nv.eight(static_cast<uint64_t>(idx), rv);
+            np_.eight(static_cast<uint64_t>(idx), rp);
+          }
+#pragma unroll
+          for (int j = 0; j < EW_VEC; ++j) {
+            const uint64_t c = static_cast<uint64_t>(idx + j);
+            adamw_one<NOISE>(vp[it].v[j], vg[it].v[j], vm[it].v[j], vv[it].v[j], hp_of<REC>(a), ss, bc2s, [&](int w) {
+              return w == 0 ? (FAST ? rm[j] : nm.at(c)) : w == 1 ? (FAST ? rv[j] : nv.at(c)) : (FAST ? rp[j] : np_.at(c));
+            });
+          }
+          if (pm)
+            mc_st_u16x8(pm + idx, vp[it]);
+          else
+            st_u16x8(p + idx, vp[it]);
+          st_u16x8(m + idx, vm[it]);
+          st_u16x8(v + idx, vv[it]);
+        } else {
+          adamw_tail<NOISE, REC>(a, E, nm, nv, np_, idx, n);
+        }
+      }
+    } else if (pm) {  // an unaligned entry with multicast weights: 4-byte pairs, thread-contiguous
+      const int64_t lo = base + static_cast<int64_t>(threadIdx.x) * (ITERS * EW_VEC);
+      adamw_tail<NOISE, REC>(a, E, nm, nv, np_, lo, lo + ITERS * EW_VEC < n ? lo + ITERS * EW_VEC : n);
+    } else {
+      for (int it = 0; it < ITERS * EW_VEC; ++it) {
+        const int64_t i = base + it * EW_THREADS + threadIdx.x;
+        if (i < n) {
+          uint16_t pb = p[i], mb = m[i], vb = v[i];
+          adamw_one<NOISE>(pb, g[i], mb, vb, hp_of<REC>(a), ss, bc2s, [&](int w) {
+              const uint64_t c = static_cast<uint64_t>(i);
+              return w == 0 ? nm.at(c) : w == 1 ? nv.at(c) : np_.at(c);
+            });
+          p[i] = pb; m[i] = mb; v[i] = vb;
+        }
+      }
     }
   }
-  __device__ bool multicast() const { return a.any_mc != 0; }
-};
-
-template <int NOISE, bool REC>
-__global__ __launch_bounds__(stream::THREADS, ADAMW_MINB) void adamw_kernel(const __grid_constant__ AdamWArgs a,
-                                                                         int* err) {
-  stream::run(AdamWPolicy<NOISE, REC>{a}, ring<4, ADAMW_STAGES>(), err);
+  if (a.any_mc) __threadfence_system();  // multicast stores ordered before the callers' barrier
 }
 
 // Gradient centralisation -- muon_sr/triton_adamw.py:179-187: out = bf16(g - c * mean), the
@@ -513,19 +537,6 @@ inline int grid_for(int64_t chunks) {
 
 inline bool record_ok(const void* rec) { return rec != nullptr && (reinterpret_cast<uintptr_t>(rec) & 15u) == 0; }
 
-// Launch of one streamed kernel instance: persistent grid of MINB CTAs per SM (at most one
-// CTA per tile), the ring in dynamic shared memory (the size attribute is set once per
-// device for each kernel function, see set_smem_attr).
-template <int NIN, int S, int MINB, class Args>
-int launch_streamed(void (*kern)(Args, int*), const Args& a, int64_t tiles, cudaStream_t st, const char* name) {
-  constexpr size_t smem = stream::smem_bytes<NIN, S>();
-  if (int status = set_smem_attr(reinterpret_cast<const void*>(kern), smem, name)) return status;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * MINB;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
-  kern<<<grid, stream::THREADS, smem, st>>>(a, device_error_word());
-  return check_launch(name);
-}
-
 // The multi-tensor launchers: entries are packed MAXE at a time (empty ones skipped, each
 // group resuming at the first entry the previous one did not take); with a record, the
 // kernels take scalars and entries from it (src[] maps packed to record indices).
@@ -539,7 +550,7 @@ int prepare_launch(const msr_prepare_entry* entries, int count, float beta, floa
     a.omb = one_minus_beta;
     a.nesterov = nesterov;
     a.rec = rec;
-    int64_t tiles = 0;
+    int64_t chunks = 0;
     int i = next;
     for (; i < count && a.count < MAXE; ++i) {
       const msr_prepare_entry& e = entries[i];
@@ -549,18 +560,19 @@ int prepare_launch(const msr_prepare_entry* entries, int count, float beta, floa
       a.e[a.count] = e;
       a.src[a.count] = i;
       a.vec[a.count] = ptr_aligned16(e.grad) && ptr_aligned16(e.momentum) && ptr_aligned16(e.update);
-      a.prefix[a.count] = tiles;
-      tiles += (e.numel + TILE - 1) / TILE;
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
       ++a.count;
     }
     next = i;
-    a.prefix[a.count] = tiles;
+    a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
     auto* kern = rec ? pick_noise(muon_prepare_kernel<NOISE_REF, true>, muon_prepare_kernel<NOISE_FAST, true>,
                                   muon_prepare_kernel<NOISE_NONE, true>)
                      : pick_noise(muon_prepare_kernel<NOISE_REF, false>, muon_prepare_kernel<NOISE_FAST, false>,
                                   muon_prepare_kernel<NOISE_NONE, false>);
-    int st = launch_streamed<2, EW_STAGES, EW_MINB>(kern, a, tiles, to_stream(stream), "muon_prepare_kernel");
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_prepare_kernel");
     if (st) return st;
   }
   return MSR_OK;
@@ -575,7 +587,7 @@ int apply_launch(const msr_apply_entry* entries, int count, float lr, float deca
     a.lr = lr;
     a.decay = decay;
     a.rec = rec;
-    int64_t tiles = 0;
+    int64_t chunks = 0;
     int i = next;
     for (; i < count && a.count < MAXE; ++i) {
       const msr_apply_entry& e = entries[i];
@@ -588,18 +600,19 @@ int apply_launch(const msr_apply_entry* entries, int count, float lr, float deca
         return fail(MSR_ERR_INVALID, "msr_muon_apply: entry %d: param_mc must have param's 16-byte alignment", i);
       a.any_mc |= e.param_mc != nullptr;
       a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.update);
-      a.prefix[a.count] = tiles;
-      tiles += (e.numel + TILE - 1) / TILE;
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + EW_CHUNK - 1) / EW_CHUNK;
       ++a.count;
     }
     next = i;
-    a.prefix[a.count] = tiles;
+    a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
     auto* kern = rec ? pick_noise(muon_apply_kernel<NOISE_REF, true>, muon_apply_kernel<NOISE_FAST, true>,
                                   muon_apply_kernel<NOISE_NONE, true>)
                      : pick_noise(muon_apply_kernel<NOISE_REF, false>, muon_apply_kernel<NOISE_FAST, false>,
                                   muon_apply_kernel<NOISE_NONE, false>);
-    int st = launch_streamed<2, EW_STAGES, EW_MINB>(kern, a, tiles, to_stream(stream), "muon_apply_kernel");
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("muon_apply_kernel");
     if (st) return st;
   }
   return MSR_OK;
@@ -614,7 +627,7 @@ int adamw_launch(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
     AdamWArgs a{};
     if (hp) a.hp = *hp;
     a.rec = rec;
-    int64_t tiles = 0;
+    int64_t chunks = 0;
     int i = next;
     for (; i < count && a.count < MAXE; ++i) {
       const msr_adamw_entry& e = entries[i];
@@ -628,18 +641,21 @@ int adamw_launch(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
       a.any_mc |= e.param_mc != nullptr;
       a.vec[a.count] = ptr_aligned16(e.param) && ptr_aligned16(e.grad) && ptr_aligned16(e.exp_avg) &&
                        ptr_aligned16(e.exp_avg_sq);
-      a.prefix[a.count] = tiles;
-      tiles += (e.numel + TILE - 1) / TILE;
+      a.prefix[a.count] = chunks;
+      chunks += (e.numel + ADAMW_CHUNK - 1) / ADAMW_CHUNK;
       ++a.count;
     }
     next = i;
-    a.prefix[a.count] = tiles;
+    a.prefix[a.count] = chunks;
     if (a.count == 0) continue;
-    auto* kern = rec ? pick_noise(adamw_kernel<NOISE_REF, true>, adamw_kernel<NOISE_FAST, true>,
-                                  adamw_kernel<NOISE_NONE, true>)
-                     : pick_noise(adamw_kernel<NOISE_REF, false>, adamw_kernel<NOISE_FAST, false>,
-                                  adamw_kernel<NOISE_NONE, false>);
-    int st = launch_streamed<4, ADAMW_STAGES, ADAMW_MINB>(kern, a, tiles, to_stream(stream), "adamw_kernel");
+    auto* kern = rec ? pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF, true>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST, true>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE, true>)
+                     : pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF, false>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST, false>,
+                                  adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE, false>);
+    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    int st = check_launch("adamw_kernel");
     if (st) return st;
   }
   return MSR_OK;
@@ -677,9 +693,10 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
   if (n < 0 || (n > 0 && (acc == nullptr || grad == nullptr)))
     return fail(MSR_ERR_INVALID, "msr_grad_accum_bf16: null pointer or negative size");
   if (n == 0) return MSR_OK;
+  const int64_t chunks = (n + EW_CHUNK - 1) / EW_CHUNK;
   const bool vec = ptr_aligned16(acc) && ptr_aligned16(grad);
   if (first) {
-    const int grid = grid_for(((n + EW_CHUNK - 1) / EW_CHUNK) * 4);
+    const int grid = grid_for(chunks * 4);
     if (vec)
       grad_accum_first_kernel<true><<<grid, EW_THREADS, 0, to_stream(stream)>>>(
           static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
@@ -688,16 +705,13 @@ int msr_grad_accum_bf16(void* acc, const void* grad, int64_t n, uint64_t key, in
           static_cast<uint16_t*>(acc), static_cast<const uint16_t*>(grad), n);
     return check_launch("grad_accum_first_kernel");
   }
-  AccumArgs a{};
-  a.acc = static_cast<uint16_t*>(acc);
-  a.g = static_cast<const uint16_t*>(grad);
-  a.n = n;
-  a.prefix[0] = 0;
-  a.prefix[1] = (n + TILE - 1) / TILE;
-  a.key = make_key(key);
-  a.vec = vec ? 1 : 0;
-  auto* kern = pick_noise(grad_accum_kernel<NOISE_REF>, grad_accum_kernel<NOISE_FAST>, grad_accum_kernel<NOISE_NONE>);
-  return launch_streamed<2, EW_STAGES, EW_MINB>(kern, a, a.prefix[1], to_stream(stream), "grad_accum_kernel");
+  auto* kern = vec ? pick_noise(grad_accum_kernel<true, NOISE_REF>, grad_accum_kernel<true, NOISE_FAST>,
+                                grad_accum_kernel<true, NOISE_NONE>)
+                  : pick_noise(grad_accum_kernel<false, NOISE_REF>, grad_accum_kernel<false, NOISE_FAST>,
+                               grad_accum_kernel<false, NOISE_NONE>);
+  kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(static_cast<uint16_t*>(acc),
+                                                               static_cast<const uint16_t*>(grad), n, make_key(key));
+  return check_launch("grad_accum_kernel");
 }
 
 int msr_muon_prepare(const msr_prepare_entry* entries, int count, float beta, float one_minus_beta, int nesterov,

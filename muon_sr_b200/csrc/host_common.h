@@ -27,10 +27,6 @@ inline cudaStream_t to_stream(msr_stream_t s) { return reinterpret_cast<cudaStre
 // once per (function, device); returns an MSR status.
 int set_smem_attr(const void* func, size_t bytes, const char* name);
 
-// Device address of the library's device error word on the current device (what
-// msr_device_error reads), for kernels that record a wait that ran out; nullptr if unknown.
-int* device_error_word();
-
 // Stochastic-rounding noise stream selected with msr_set_sr_noise (an msr_sr_noise value).
 int sr_noise_mode();
 

@@ -997,24 +997,6 @@ NsLayout ns_layout(int64_t batch, int64_t rows, int64_t cols) {
 }  // namespace gemm
 }  // namespace msr
 
-namespace msr {
-// Device address of g_msr_device_error on the current device, for kernels of other
-// translation units (which cannot name the symbol without relocatable device code); looked
-// up once per device. nullptr if the lookup fails (those kernels then record nothing).
-int* device_error_word() {
-  static std::mutex mu;
-  static int* cached[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_msr_device_error) != cudaSuccess) return nullptr;
-    cached[dev] = static_cast<int*>(p);
-  }
-  return cached[dev];
-}
-}  // namespace msr
 
 using namespace msr;
 using namespace msr::gemm;
