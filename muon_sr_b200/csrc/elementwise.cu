@@ -22,7 +22,7 @@ namespace {
 constexpr int EW_THREADS = 256;
 constexpr int EW_VEC = 8;
 constexpr int EW_ITERS = 2;
-constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 8192 elements
+constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 4096 elements
 constexpr int MAXE = 64;
 constexpr int EW_BLOCKS_PER_SM = 4;
 // AdamW: 2 vectors of 8 per thread and chunk at 2 CTAs per SM measured faster (1425 GB/s on
