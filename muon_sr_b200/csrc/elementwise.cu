@@ -2,7 +2,7 @@
 // prepare (momentum + Nesterov), Muon apply (decay + scaled update) and AdamW-SR.
 //
 // Design (B200): multi-tensor launches. Each launch carries up to MAXE tensors in its
-// kernel parameters; the work is cut into chunks of 8192 elements that never cross a
+// kernel parameters; the work is cut into chunks of 4096 elements that never cross a
 // tensor, and a persistent grid (a multiple of the SM count) walks the chunks. Each thread
 // moves 8 bf16 per 16-byte access, issuing all loads of a chunk before its math so that
 // every SM keeps enough bytes in flight for HBM3e. All fp32 arithmetic uses explicit
