@@ -875,7 +875,7 @@ def main():
                     help="with --kernel ns: the stack as BATCHxROWSxCOLS (e.g. 12x768x3072)")
     ap.add_argument("--noise", choices=["reference", "fast", "none"], default="reference",
                     help="with --kernel: the stochastic-rounding noise stream")
-    ap.add_argument("--transport", choices=["auto", "multicast", "p2p", "nccl"], default="p2p",
+    ap.add_argument("--transport", choices=["auto", "multicast", "p2p", "nccl"], default="auto",
                     help="N>1: how the sharded step shares the updated weights (Sharder transport)")
     ap.add_argument("--reserve-sms", type=int, default=int(os.environ.get("MSR_RESERVE_SMS", "0")),
                     help="N>1: SMs the GEMMs leave to the concurrent weight broadcasts")
