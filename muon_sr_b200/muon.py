@@ -14,6 +14,8 @@ update, SR weights). With ``batch_ns`` the momentum of equal-shaped matrices liv
 stack and Newton-Schulz runs on chunks of the stack. ``shard`` (optional) spreads the work
 over the ranks of a process group (see ``sharding``).
 """
+import contextlib
+
 import torch
 from torch.optim import Optimizer
 
@@ -21,6 +23,8 @@ from . import kernels as K
 from . import staging
 from .adamw import adamw_group_step
 from .seeds import deterministic_seed
+
+_nullctx = contextlib.nullcontext
 
 # Max elements per batched Newton-Schulz call, as in the reference (triton_muon_sr.py:125).
 # Each matrix is computed independently, so the bits do not depend on the chunking. Larger
@@ -163,10 +167,11 @@ def _segments(n, count):
 class _Work:
     """Where a batched step may do its work: ``owner(stack_idx, row) -> bool`` (None = all),
     ``share(params)`` after each stack / segment and ``segments(shape, n)`` (None = whole
-    stacks), all from a ``sharding.Sharder``."""
+    stacks), all from a ``sharding.Sharder``; ``side``: a stream on which the weight updates
+    (apply) run after their chunk's Newton-Schulz, overlapping the next chunk (None: in line)."""
 
-    def __init__(self, owner=None, share=None, segments=None):
-        self.owner, self.share, self.segments = owner, share, segments
+    def __init__(self, owner=None, share=None, segments=None, side=None):
+        self.owner, self.share, self.segments, self.side = owner, share, segments, side
 
     def mine(self, stack_idx, row):
         return self.owner is None or self.owner(stack_idx, row)
@@ -275,8 +280,20 @@ def _stack_step(s, shape, members, momentum, beta, nesterov, ns_steps, lr, weigh
             K.muon_prepare([(_grad_of(p), momentum[rows[c + j]], x[j], rows[c + j] * numel, prep_seed)
                             for j, p in enumerate(mine)], beta, nesterov)
             out = K.newton_schulz(x, ns_steps)
-            K.muon_apply([(p, out[j], scale, apply_seed[rows[c + j]]) for j, p in enumerate(mine)], lr, weight_decay)
-            staging.done(mine)
+            items = [(p, out[j], scale, apply_seed[rows[c + j]]) for j, p in enumerate(mine)]
+            if work.side is not None:
+                # the weight update on the side stream: it waits for this chunk's Newton-Schulz
+                # only, so its (multicast) stores overlap the next chunk's GEMMs
+                ns_done = torch.cuda.Event()
+                ns_done.record()
+                with torch.cuda.stream(work.side):
+                    work.side.wait_event(ns_done)
+                    out.record_stream(work.side)
+                    K.muon_apply(items, lr, weight_decay)
+                    staging.done(mine)
+            else:
+                K.muon_apply(items, lr, weight_decay)
+                staging.done(mine)
             del out
         lo = hi
         if len(parts) > 1:
@@ -371,7 +388,7 @@ class _MuonBase(Optimizer):
             for p in group["params"]:
                 _validate(p, name)
             step = self._clock.advance(self.state, batched_groups, group["params"]) if self._record_step else 0
-            work = _Work(sh.muon_owner(gi, stacks.by_shape), sh.share, sh.segments) if sh else None
+            work = _Work(sh.muon_owner(gi, stacks.by_shape), sh.share, sh.segments, sh.update_stream) if sh else None
             muon_batch_step(stacks, beta, nesterov, ns_steps, lr, wd, step, seeder, work)
             return
         for i, p in enumerate(group["params"]):
@@ -489,8 +506,11 @@ class TritonMuonSRWithAuxAdam(_MuonBase):
                 if group["params"]:
                     self._run_muon_group(gi, group, self.batch_ns, muon_groups, seeder)
                 continue
-            adamw_group_step(self.state, group, offsets[gi], lambda step, idx: seeder(step, idx, 0),
-                             owns=(lambda i, gi=gi: sh.owns(gi, i)) if sh else None)
+            side = sh.update_stream if sh else None
+            with torch.cuda.stream(side) if side is not None else _nullctx():
+                # (multicast weights: the AdamW updates run under the Muon groups' GEMMs)
+                adamw_group_step(self.state, group, offsets[gi], lambda step, idx: seeder(step, idx, 0),
+                                 owns=(lambda i, gi=gi: sh.owns(gi, i)) if sh else None)
             if sh:
                 sh.share(group["params"])
         if sh:

@@ -35,7 +35,7 @@ import torch.distributed as dist
 # reference's Philox noise stream, well below the HBM copy rate.
 TENSOR_FLOPS = 1.7e15
 MUON_EW_BYTES = 2.0e12     # prepare (8 B) + apply (6 B) per element
-ADAMW_BYTES = 1.0e12       # 14 B per element, three Philox streams
+ADAMW_BYTES = 1.2e12       # 14 B per element, three Philox streams (1.25e12 measured at 8 GPUs)
 ADAMW8BIT_BYTES = 1.28e12  # 10.0625 B per element
 SEGMENT_SECONDS = 4e-3  # per-rank Newton-Schulz time between two weight shares of a stack
 COPY_STREAMS_PER_PEER = 2
@@ -128,6 +128,7 @@ class Sharder:
         self._order = None  # params in a fixed order
         self._p2p = None    # lazily built peer mappings
         self._mc = None     # lazily built multicast weights
+        self._side = None   # stream of the weight updates under the multicast transport
 
     # -- plan -----------------------------------------------------------------------------
     def plan(self, param_groups):
@@ -201,6 +202,15 @@ class Sharder:
         per_rank = n * _ns_flops(tuple(shape)) / TENSOR_FLOPS / self.world
         return max(1, min(8, n // (2 * self.world), round(per_rank / SEGMENT_SECONDS)))
 
+    @property
+    def update_stream(self):
+        """Under the multicast transport, the stream on which the optimizers run the weight
+        updates (apply after each chunk's Newton-Schulz, the AdamW groups) so that their
+        NVLink multicast stores overlap the Newton-Schulz GEMMs on the current stream; it
+        starts after the step's start point and the step's end point waits for it. None with
+        the other transports (their updates run in line and the copies overlap instead)."""
+        return self._side if self.transport == "multicast" else None
+
     def owns(self, gi, pi) -> bool:
         return self._owner[id(self._groups[gi]["params"][pi])] == self.rank
 
@@ -215,6 +225,9 @@ class Sharder:
         self._point = 0
         if self.transport == "multicast":
             self._mc.begin()
+            if self._side is None:
+                self._side = torch.cuda.Stream(self._mc.device)
+            self._side.wait_stream(torch.cuda.current_stream(self._mc.device))
 
     def share(self, params):
         """Start sharing each of ``params`` that has a gradient from its owner. Every rank
@@ -241,6 +254,7 @@ class Sharder:
         this step's transfers."""
         self.share(self._order)
         if self.transport == "multicast":
+            torch.cuda.current_stream(self._mc.device).wait_stream(self._side)
             self._mc.finish()
             return
         if self.transport == "p2p":
