@@ -210,23 +210,6 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, i
   }
 }
 
-// Before a tile's accumulator is ready, each epilogue thread asks L2 for its row's share of
-// the C operand (128 columns, 256 bytes), so that the epilogue's chunked C loads hit L2
-// instead of waiting for HBM: the C operand does not depend on the accumulator, and the
-// prefetch runs under the tile's main loop. Only in-range addresses are prefetched.
-__device__ __forceinline__ void epilogue_prefetch_c(const Params& p, int64_t b, int64_t row0, int64_t n0, int q, int h,
-                                                    int lane) {
-  if (p.c == nullptr || p.beta == 0.f) return;
-  const int64_t row = row0 + q * 32 + lane;
-  if (row >= p.M) return;
-  const int64_t c0 = n0 + h * (BN / 2);
-  const uint16_t* crow = p.c + b * p.c_bstride + row * p.ldc;
-#pragma unroll
-  for (int k = 0; k < BN / 2; k += 64) {  // one 128-byte line per 64 columns
-    if (c0 + k < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(crow + c0 + k));
-  }
-}
-
 // One epilogue warp's share of a finished tile: TMEM lane quarter q (rows row0 + 32 q +
 // lane) and column half h of the 256-column accumulator at tmem_acc, with the next chunk's
 // TMEM read and C-operand loads in flight under the current chunk's math.
@@ -424,14 +407,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int64_t b, m0, n0;
-      decode_tile<BM>(p, t, b, m0, n0);
-      epilogue_prefetch_c(p, b, m0, n0, q, h, lane);
       if (!tc::mbar_wait(&S.tmem_full[acc], acc_phase, abort, WAIT_LIMIT_NS)) {
         record_error(ERR_EPI_WAIT);
         break;
       }
       tc::fence_after_sync();
+      int64_t b, m0, n0;
+      decode_tile<BM>(p, t, b, m0, n0);
       epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane);
       tc::fence_before_sync();
       tc::mbar_arrive(&S.tmem_empty[acc]);
@@ -667,14 +649,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int64_t t = pair_id; t < p.num_tiles; t += num_pairs) {
-      int64_t b, m0, n0;
-      decode_tile<TILE_M>(p, t, b, m0, n0);
-      epilogue_prefetch_c(p, b, m0 + HALF * rank, n0, q, h, lane);
       if (!tc::mbar_wait(&S.tmem_full[acc], acc_phase, abort, WAIT_LIMIT_NS)) {
         give_up(ERR_EPI_WAIT);
         break;
       }
       tc::fence_after_sync();
+      int64_t b, m0, n0;
+      decode_tile<TILE_M>(p, t, b, m0, n0);
       epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane);
       tc::fence_before_sync();
       __syncwarp();
