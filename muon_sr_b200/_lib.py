@@ -9,6 +9,8 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmuon_sr_b200.so")
+# msr_abi_version() of the library these bindings describe (the entry structs below)
+ABI_VERSION = 2
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int

@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exists_and_loads():
     assert os.path.exists(_lib.LIB_PATH), "build the library first: python -m muon_sr_b200.build"
     lib = _lib.load()
-    assert lib.msr_abi_version() == 2
+    assert lib.msr_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
