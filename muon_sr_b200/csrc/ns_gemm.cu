@@ -211,17 +211,11 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, i
 }
 
 // One epilogue warp's share of a finished tile: TMEM lane quarter q (rows row0 + 32 q +
-// lane) and column half h of the 256-column accumulator at tmem_acc. The C operand (the
-// beta * C term) is read CLA chunks ahead of the chunk being computed -- a ring of CLA + 1
-// chunk buffers -- so that several global loads per thread are in flight while the TMEM
-// reads and the math of the current chunk proceed. CLA = 1 (128 registers) for GEMMs with a
-// long main loop, which hides the epilogue; CLA = 3 (about 160 registers) when K is short and
-// the epilogue, waiting on load latency, sets the pace (see run_gemm).
-template <int CLA>
+// lane) and column half h of the 256-column accumulator at tmem_acc, with the next chunk's
+// TMEM read and C-operand loads in flight under the current chunk's math.
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int64_t b, int64_t row0, int64_t n0,
                                               int q, int h, int lane) {
   constexpr int CHUNKS = BN / 2 / EPI_CW;
-  constexpr int RING = CLA + 1;
   float alpha = p.alpha, beta = p.beta;
   if (p.scale != nullptr) {
     float s = p.scale[b];
@@ -240,30 +234,31 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc
   const int64_t cbase = n0 + h * (BN / 2);
   const uint32_t tbase = tmem_acc + static_cast<uint32_t>(h * (BN / 2)) + (static_cast<uint32_t>(q * 32) << 16);
   uint32_t v[EPI_CW], vn[EPI_CW];
-  U16x8 cring[RING][EPI_G];
+  U16x8 cv[EPI_G], cvn[EPI_G];
   __syncwarp();
   tc::tmem_ld_32x32b_x16(tbase, v);
-#pragma unroll
-  for (int k = 0; k < RING && k < CHUNKS; ++k) load_c_chunk(p, er, cbase + k * EPI_CW, cring[k]);
+  load_c_chunk(p, er, cbase, cv);
   tc::tmem_ld_wait();
 #pragma unroll
   for (int cc = 0; cc < CHUNKS; ++cc) {
     if (cc + 1 < CHUNKS) {
       __syncwarp();
       tc::tmem_ld_32x32b_x16(tbase + (cc + 1) * EPI_CW, vn);
+      load_c_chunk(p, er, cbase + (cc + 1) * EPI_CW, cvn);
     }
-    store_chunk(p, er, cbase + cc * EPI_CW, v, cring[cc % RING], alpha, beta);
-    if (cc + RING < CHUNKS) load_c_chunk(p, er, cbase + (cc + RING) * EPI_CW, cring[cc % RING]);
+    store_chunk(p, er, cbase + cc * EPI_CW, v, cv, alpha, beta);
     if (cc + 1 < CHUNKS) {
       tc::tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < EPI_CW; ++j) v[j] = vn[j];
+#pragma unroll
+      for (int j = 0; j < EPI_G; ++j) cv[j] = cvn[j];
     }
   }
   __syncwarp();
 }
 
-template <int A_MN, int B_MN, int CLA>
+template <int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -419,7 +414,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc::fence_after_sync();
       int64_t b, m0, n0;
       decode_tile<BM>(p, t, b, m0, n0);
-      epilogue_tile<CLA>(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane);
       tc::fence_before_sync();
       tc::mbar_arrive(&S.tmem_empty[acc]);
       if (++acc == 2) {
@@ -501,7 +496,7 @@ __device__ __forceinline__ void settle(uint64_t ns) {
   } while (t - t0 < ns);
 }
 
-template <int A_MN, int B_MN, int CLA>
+template <int A_MN, int B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   using pair::HALF;
@@ -661,7 +656,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc::fence_after_sync();
       int64_t b, m0, n0;
       decode_tile<TILE_M>(p, t, b, m0, n0);
-      epilogue_tile<CLA>(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(leader_empty[acc]);
@@ -740,13 +735,13 @@ int smem_attr_once(K kern, int smem, std::atomic<int>* done_per_device) {
   return MSR_OK;
 }
 
-std::atomic<int> g_single_attr[8][MAX_DEVICES];  // [variant: A_MN * 2 + B_MN + 4 * (CLA > 1)]
-std::atomic<int> g_pair_attr[8][MAX_DEVICES];
+std::atomic<int> g_single_attr[4][MAX_DEVICES];
+std::atomic<int> g_pair_attr[4][MAX_DEVICES];
 
-template <int A_MN, int B_MN, int CLA>
+template <int A_MN, int B_MN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
-  auto kern = gemm_kernel<A_MN, B_MN, CLA>;
-  if (int st = smem_attr_once(kern, (int)smem_bytes(), g_single_attr[A_MN * 2 + B_MN + 4 * (CLA > 1)])) return st;
+  auto kern = gemm_kernel<A_MN, B_MN>;
+  if (int st = smem_attr_once(kern, (int)smem_bytes(), g_single_attr[A_MN * 2 + B_MN])) return st;
   int ctas = sm_count();
   const int cap = g_gemm_max_ctas.load(std::memory_order_relaxed);
   if (cap > 0 && cap < ctas) ctas = cap;
@@ -761,13 +756,13 @@ std::atomic<int> g_gemm_pairs{1};
 
 // Clusters of two that fit on the device at once (a GPC with an odd number of free SMs
 // leaves one idle), per kernel variant and device.
-std::atomic<int> g_pair_capacity[8][MAX_DEVICES];
+std::atomic<int> g_pair_capacity[4][MAX_DEVICES];
 
-template <int A_MN, int B_MN, int CLA>
+template <int A_MN, int B_MN>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t s) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN, CLA>;
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
   const int smem = static_cast<int>(pair_smem_bytes());
-  if (int st = smem_attr_once(kern, smem, g_pair_attr[A_MN * 2 + B_MN + 4 * (CLA > 1)])) return st;
+  if (int st = smem_attr_once(kern, smem, g_pair_attr[A_MN * 2 + B_MN])) return st;
   cudaError_t e;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -782,7 +777,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, c
   cfg.numAttrs = 1;
   int dev = 0;
   cudaGetDevice(&dev);
-  std::atomic<int>& cap_slot = g_pair_capacity[A_MN * 2 + B_MN + 4 * (CLA > 1)][dev % MAX_DEVICES];
+  std::atomic<int>& cap_slot = g_pair_capacity[A_MN * 2 + B_MN][dev % MAX_DEVICES];
   int pairs = cap_slot.load(std::memory_order_relaxed);
   if (pairs <= 0) {
     cfg.gridDim = dim3(2 * (sm_count() / 2));
@@ -821,23 +816,6 @@ void set_tiles(Params& p, int64_t M, int64_t N, int64_t batch, int sym, int64_t 
 // D[b] = alpha_b * op(A)[b] x op(B)[b]^T + beta_b * C[b]. A K-major: [batch][M][K]; MN-major:
 // [batch][K][M]. B K-major: [batch][N][K]; MN-major: [batch][K][N]. C, D: [batch][M][N] with
 // row strides ldc, ldd.
-constexpr int64_t EPI_DEEP_MAX_K = 1024;
-
-template <int CLA>
-int launch_cla(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, bool pairs, int a_mn, int b_mn,
-               cudaStream_t s) {
-  if (pairs) {
-    if (a_mn && b_mn) return launch_pair<1, 1, CLA>(ta, tb, p, s);
-    if (a_mn) return launch_pair<1, 0, CLA>(ta, tb, p, s);
-    if (b_mn) return launch_pair<0, 1, CLA>(ta, tb, p, s);
-    return launch_pair<0, 0, CLA>(ta, tb, p, s);
-  }
-  if (a_mn && b_mn) return launch<1, 1, CLA>(ta, tb, p, s);
-  if (a_mn) return launch<1, 0, CLA>(ta, tb, p, s);
-  if (b_mn) return launch<0, 1, CLA>(ta, tb, p, s);
-  return launch<0, 0, CLA>(ta, tb, p, s);
-}
-
 int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn, int64_t b_bstride, const void* c,
          int64_t ldc, int64_t c_bstride, void* d, int64_t ldd, int64_t d_bstride, int64_t batch, int64_t M, int64_t N,
          int64_t K, float alpha, float beta, const float* scale, int alpha_pow, int beta_pow, int scale_is_norm_sq,
@@ -861,11 +839,16 @@ int run_gemm(const void* a, int a_mn, int64_t a_bstride, const void* b, int b_mn
   p.alpha = alpha; p.beta = beta;
   p.scale = scale; p.alpha_pow = alpha_pow; p.beta_pow = beta_pow; p.scale_is_norm_sq = scale_is_norm_sq;
   p.ref_round = ref_round;
-  // Short main loops (K <= 1024: 16 k-blocks or fewer) cannot hide the epilogue: those GEMMs
-  // take the variant that keeps three C-operand chunks in flight (more registers per thread).
-  // Both variants compute the same bits.
-  if (K <= EPI_DEEP_MAX_K) return launch_cla<3>(ta, tb, p, pairs, a_mn, b_mn, s);
-  return launch_cla<1>(ta, tb, p, pairs, a_mn, b_mn, s);
+  if (pairs) {
+    if (a_mn && b_mn) return launch_pair<1, 1>(ta, tb, p, s);
+    if (a_mn) return launch_pair<1, 0>(ta, tb, p, s);
+    if (b_mn) return launch_pair<0, 1>(ta, tb, p, s);
+    return launch_pair<0, 0>(ta, tb, p, s);
+  }
+  if (a_mn && b_mn) return launch<1, 1>(ta, tb, p, s);
+  if (a_mn) return launch<1, 0>(ta, tb, p, s);
+  if (b_mn) return launch<0, 1>(ta, tb, p, s);
+  return launch<0, 0>(ta, tb, p, s);
 }
 
 // ---------------------------------------------------------------------------------------
