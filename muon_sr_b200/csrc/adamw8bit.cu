@@ -79,9 +79,11 @@ __device__ __forceinline__ uint32_t quantize_table(float x, const uint8_t* __res
   const uint32_t ab = __float_as_uint(x) & 0x7FFFFFFFu;
   const int b = min(max(static_cast<int>(ab >> 15) - MSR_QT_BASE, 0), MSR_QT_NB - 1);
   const float ax = __uint_as_float(ab);
-  if (SIGNED && x < 0.f) {
-    const int c = codes_neg[b];
-    return static_cast<uint32_t>(c - (ax >= T_neg[c] ? 1 : 0));
+  if (SIGNED) {  // one lookup per table, its side picked by the index
+    const bool neg = x < 0.f;
+    const int c = codes_pos[b + (neg ? static_cast<int>(codes_neg - codes_pos) : 0)];
+    const int hit = ax >= T_pos[c + (neg ? static_cast<int>(T_neg - T_pos) : 0)] ? 1 : 0;
+    return static_cast<uint32_t>(neg ? c - hit : c + hit);
   }
   const int c = codes_pos[b];
   return static_cast<uint32_t>(c + (ax >= T_pos[c] ? 1 : 0));
@@ -152,14 +154,16 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
   __syncthreads();
   const msr_adamw8bit_hparams hp = a.hp;
   const int64_t total = a.prefix[a.count];
+  int ei = blockIdx.x < total ? find_entry<Q_MAXE>(a.prefix, a.count, blockIdx.x) : 0;
   for (int64_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
-    const int ei = find_entry<Q_MAXE>(a.prefix, a.count, tile);
+    while (a.prefix[ei + 1] <= tile) ++ei;  // tiles only move forward; prefix[count] = total
     const msr_adamw8bit_entry& E = a.e[ei];
     const int64_t n = E.numel;
     const int64_t base = (tile - a.prefix[ei]) * TILE + static_cast<int64_t>(threadIdx.x) * EPT;
     uint16_t* P = static_cast<uint16_t*>(E.param);
     const uint16_t* Gp = static_cast<const uint16_t*>(E.grad);
     const bool vec = a.vec[ei] && base + EPT <= n;
+    const int nvalid = vec ? EPT : (n - base >= EPT ? EPT : (n > base ? static_cast<int>(n - base) : 0));
     const SrNoise<NOISE> np_{make_key(E.key_p)};
 
     uint16_t pb[EPT], gb[EPT];
@@ -250,7 +254,7 @@ __global__ __launch_bounds__(Q_THREADS, 4) void adamw8bit_kernel(const __grid_co
       const float upd = fsub(p, __fdiv_rn(fmul(E.coef, m[j]), fadd(__fsqrt_rn(v[j]), E.sqrt_bc2_eps)));
       const float updated = fmul(upd, hp.decay);
       if (fin) pb[j] = round_bf16<NOISE>(updated, FAST ? rp[j] : np_.at(static_cast<uint64_t>(base + j)));
-      if (base + j < n) {
+      if (j < nvalid) {
         mmax = fmaxf(mmax, fabsf(m[j]));
         vmax = fmaxf(vmax, fabsf(v[j]));
       }

@@ -25,10 +25,11 @@ constexpr int EW_ITERS = 2;
 constexpr int64_t EW_CHUNK = EW_THREADS * EW_VEC * EW_ITERS;  // 4096 elements
 constexpr int MAXE = 64;
 constexpr int EW_BLOCKS_PER_SM = 4;
-// AdamW: 2 vectors of 8 per thread and chunk at 2 CTAs per SM measured faster (1425 GB/s on
-// 2^28 elements) than 1 vector at 4 CTAs per SM (1368 GB/s), where the three Philox chains per
-// element no longer fit the 64-register budget.
-constexpr int ADAMW_ITERS = 2;
+// AdamW: the three Philox chains of each element need more than 64 registers. Measured on 2^30
+// elements with the reference noise: 1 vector of 8 per thread and chunk at 2 CTAs per SM
+// (122 registers, no spills) 1645 GB/s; 2 vectors at 2 CTAs per SM (128 registers, 40 bytes
+// of spills) 1490; 1 vector at 3 or 4 CTAs per SM (80 / 64 registers, spilling) slower still.
+constexpr int ADAMW_ITERS = 1;
 constexpr int ADAMW_MINB = 2;
 constexpr int64_t ADAMW_CHUNK = EW_THREADS * EW_VEC * ADAMW_ITERS;
 
@@ -654,7 +655,10 @@ int adamw_launch(const msr_adamw_entry* entries, int count, const msr_adamw_hpar
                      : pick_noise(adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_REF, false>,
                                   adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_FAST, false>,
                                   adamw_kernel<ADAMW_ITERS, ADAMW_MINB, NOISE_NONE, false>);
-    kern<<<grid_for(chunks), EW_THREADS, 0, to_stream(stream)>>>(a);
+    // one wave of resident CTAs (ADAMW_MINB per SM), each walking its chunks
+    const int64_t cap = static_cast<int64_t>(sm_count()) * ADAMW_MINB;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(chunks, cap)));
+    kern<<<grid, EW_THREADS, 0, to_stream(stream)>>>(a);
     int st = check_launch("adamw_kernel");
     if (st) return st;
   }
