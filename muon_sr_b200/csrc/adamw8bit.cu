@@ -9,8 +9,8 @@
 //
 // Design (B200): each thread owns 8 consecutive elements (16-byte weight/gradient loads,
 // 8-byte code loads); a quantisation block of BS elements is BS/8 consecutive threads, so
-// the block absmax is a warp-shuffle reduction (plus shared memory when a block spans
-// warps). Both codebooks live in shared memory. A persistent grid walks tiles of
+// the block absmax is a warp reduction (one redux.sync for a whole warp, shuffles for
+// smaller blocks, plus shared memory when a block spans warps). Both codebooks live in shared memory. A persistent grid walks tiles of
 // 256 threads x 8 (or x16 for BS = 4096) elements across all tensors of the launch.
 #include "common.cuh"
 #include "host_common.h"
@@ -100,15 +100,18 @@ __device__ __forceinline__ float div_by_recip(float x, float d, float r) {
 __device__ __forceinline__ bool finite_f(float g) { return fabsf(g) < __int_as_float(0x7f800000); }
 
 // Max-reduce over groups of G consecutive threads (G a power of two, <= Q_THREADS).
+// v >= 0 and not NaN (a thread's fmaxf over |values| starting from 0), so the order of the
+// bit patterns as unsigned integers is the order of the values.
 template <int G>
 __device__ __forceinline__ float group_max(float v, float* red) {
-  if constexpr (G <= 32) {
+  if constexpr (G == 32) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+  } else if constexpr (G < 32) {
 #pragma unroll
     for (int o = G / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
   } else {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    v = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
     const int w = threadIdx.x >> 5;
     __syncthreads();
     if ((threadIdx.x & 31) == 0) red[w] = v;
