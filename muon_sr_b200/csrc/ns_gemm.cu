@@ -41,6 +41,12 @@ constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
+// Epilogue chunking and staging (see the epilogue helpers below).
+constexpr int EPI_CW = 32;                    // columns per epilogue chunk
+constexpr int EPI_G = EPI_CW / 8;             // 16-byte groups per chunk row
+constexpr int EPI_ROW_BYTES = EPI_CW * 2;     // 64
+constexpr int EPI_STAGE_BYTES = 32 * EPI_ROW_BYTES;  // one warp's buffer: 2 KB
+constexpr int EPI_WARPS = EPI_THREADS / 32;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // 1 s: far above any legitimate wait
 
 // Error codes recorded in g_msr_device_error (role of the wait that expired).
@@ -48,6 +54,7 @@ constexpr int ERR_TMA_WAIT = 0x101, ERR_MMA_WAIT = 0x102, ERR_EPI_WAIT = 0x103;
 
 struct SharedStorage {
   alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  alignas(16) uint8_t epi[EPI_WARPS][EPI_STAGE_BYTES];  // epilogue staging, one buffer per warp
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
@@ -140,70 +147,109 @@ __host__ __device__ __forceinline__ void decode_tile(const Params& p, int64_t t,
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device_error, 0, code); }
 
-// One epilogue thread's output row of the current tile.
-struct EpiRow {
-  uint16_t* d;           // output matrix
-  uint16_t* drow;        // its row `row`
-  const uint16_t* crow;  // C operand row, or null when beta * C is not used
-  int64_t row;
-  bool ok;               // row < M
+// Epilogue data movement. A warp owns 32 rows of the tile (its TMEM lane quarter) and walks
+// its 128 columns in chunks of 32. The accumulator arrives one row per thread (tcgen05.ld
+// 32x32b), which would make every global access of a warp touch 32 rows; instead the C
+// operand and the output pass through a 2 KB staging buffer per warp in shared memory, so
+// that each global access instruction covers 8 rows x 64 contiguous bytes (lane l moves the
+// 16-byte group l % 4 of row l / 4 + 8 i in pass i). The buffer holds 32 rows of 64 bytes;
+// group g of row r sits at slot g ^ ((r >> 1) & 3), which keeps both access patterns (8
+// lanes reading 8 rows at one group; 8 lanes writing 2 rows x 4 groups) free of bank
+// conflicts.
+
+__device__ __forceinline__ uint4* epi_slot(uint8_t* stage, int r, int g) {
+  return reinterpret_cast<uint4*>(stage + r * EPI_ROW_BYTES + ((g ^ ((r >> 1) & 3)) << 4));
+}
+
+// The warp's view of one output tile: rows [rbase, rbase + 32) of matrix b, and this lane's
+// own row (used by the math and by the mirror stores of symmetric tiles).
+struct EpiRows {
+  uint16_t* d;           // output matrix b
+  const uint16_t* c;     // C operand matrix b, or null when beta * C is not used
+  int64_t rbase;         // first row of the warp
+  int64_t row;           // this lane's row, rbase + lane
 };
 
-constexpr int EPI_CW = 16;               // columns per epilogue chunk
-constexpr int EPI_G = EPI_CW / 8;         // 16-byte groups per chunk
-
-// C operand for columns [col0, col0 + EPI_CW) of this row (zeros where unused / out of range).
-__device__ __forceinline__ void load_c_chunk(const Params& p, const EpiRow& er, int64_t col0, U16x8 (&cv)[EPI_G]) {
+// C operand for columns [col0, col0 + EPI_CW) of the warp's 32 rows, coalesced pattern:
+// creg[i] = row rbase + 8 i + lane / 4, columns col0 + 8 (lane % 4) .. + 7 (zeros outside).
+__device__ __forceinline__ void load_c_coalesced(const Params& p, const EpiRows& er, int64_t col0, int lane,
+                                                 uint4 (&creg)[4]) {
+  const int64_t col = col0 + (lane & 3) * 8;
 #pragma unroll
-  for (int g = 0; g < EPI_G; ++g) {
-    const int64_t col = col0 + g * 8;
-    if (er.crow != nullptr && er.ok && col + 8 <= p.N) {
-      cv[g] = ld_u16x8(er.crow + col);
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = er.rbase + i * 8 + (lane >> 2);
+    if (row < p.M && col + 8 <= p.N) {
+      creg[i] = *reinterpret_cast<const uint4*>(er.c + row * p.ldc + col);
     } else {
+      U16x8 t;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        cv[g].v[j] = (er.crow != nullptr && er.ok && col + j < p.N) ? er.crow[col + j] : uint16_t(0);
+      for (int j = 0; j < 8; ++j) t.v[j] = (row < p.M && col + j < p.N) ? er.c[row * p.ldc + col + j] : uint16_t(0);
+      creg[i] = *reinterpret_cast<const uint4*>(t.v);
     }
   }
 }
 
-// Epilogue math and stores for columns [col0, col0 + EPI_CW) of this row.
-__device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, int64_t col0,
-                                            const uint32_t (&v)[EPI_CW], const U16x8 (&cv)[EPI_G], float alpha,
-                                            float beta) {
-  if (!er.ok || col0 >= p.N) return;
+// Coalesced C registers -> staging buffer (row r of the warp at row r of the buffer).
+__device__ __forceinline__ void c_to_stage(uint8_t* stage, const uint4 (&creg)[4], int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) *epi_slot(stage, i * 8 + (lane >> 2), lane & 3) = creg[i];
+}
+
+// Epilogue math for this lane's row, columns [col0, col0 + EPI_CW), in place in the staging
+// buffer: each 16-byte group of the row is read (the C operand, when used) and overwritten
+// with the output by this lane alone.
+__device__ __forceinline__ void chunk_math(const Params& p, bool use_c, const uint32_t (&v)[EPI_CW], float alpha,
+                                           float beta, uint8_t* stage, int lane) {
 #pragma unroll
   for (int g = 0; g < EPI_G; ++g) {
-    const int64_t col = col0 + g * 8;
-    if (col >= p.N) break;
-    U16x8 o;
+    uint4* slot = epi_slot(stage, lane, g);
+    U16x8 cv, o;
+    if (use_c) *reinterpret_cast<uint4*>(cv.v) = *slot;
     if (p.ref_round) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float t = bf16r(__fmul_rn(alpha, bf16r(__uint_as_float(v[g * 8 + j]))));
-        o.v[j] = er.crow != nullptr
-                     ? rne_bf16_bits(__fadd_rn(bf16r(__fmul_rn(beta, bf16_bits_to_f32(cv[g].v[j]))), t))
-                     : rne_bf16_bits(t);
+        o.v[j] = use_c ? rne_bf16_bits(__fadd_rn(bf16r(__fmul_rn(beta, bf16_bits_to_f32(cv.v[j]))), t))
+                       : rne_bf16_bits(t);
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        o.v[j] = rne_bf16_bits(fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * bf16_bits_to_f32(cv[g].v[j])));
+        o.v[j] = rne_bf16_bits(fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * (use_c ? bf16_bits_to_f32(cv.v[j]) : 0.f)));
     }
-    if (col + 8 <= p.N) {
-      st_u16x8(er.drow + col, o);
-    } else {
+    *slot = *reinterpret_cast<const uint4*>(o.v);
+  }
+}
+
+// The chunk's output rows in the staging buffer -> coalesced stores of the warp's 32 rows;
+// then, in symmetric mode, the mirror of the strictly-upper elements: (row, c) -> (c, row).
+// Lanes hold consecutive rows, so each mirrored column's stores form one 64-byte segment.
+__device__ __forceinline__ void store_chunk(const Params& p, const EpiRows& er, uint8_t* stage, int64_t col0,
+                                            int lane) {
+  const int64_t col = col0 + (lane & 3) * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const int64_t row = er.rbase + r;
+    const uint4 w = *epi_slot(stage, r, lane & 3);
+    if (row < p.M && col + 8 <= p.N) {
+      *reinterpret_cast<uint4*>(er.d + row * p.ldd + col) = w;
+    } else if (row < p.M) {
+      const uint16_t* wv = reinterpret_cast<const uint16_t*>(&w);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (col + j < p.N) er.drow[col + j] = o.v[j];
+        if (col + j < p.N) er.d[row * p.ldd + col + j] = wv[j];
     }
-    if (p.sym && col + 7 > er.row) {
-      // Mirror the strictly-upper elements: (row, c) -> (c, row). Lanes hold consecutive
-      // rows, so each column's stores form one 64-byte segment.
-      uint16_t* dcol = er.d + er.row;
+  }
+  if (p.sym && er.row < p.M && col0 + EPI_CW - 1 > er.row) {
+    uint16_t* dcol = er.d + er.row;
+#pragma unroll
+    for (int g = 0; g < EPI_G; ++g) {
+      U16x8 o;
+      *reinterpret_cast<uint4*>(o.v) = *epi_slot(stage, lane, g);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int64_t c = col + j;
+        const int64_t c = col0 + g * 8 + j;
         if (c > er.row && c < p.N) dcol[c * p.ldd] = o.v[j];
       }
     }
@@ -212,9 +258,9 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRow& er, i
 
 // One epilogue warp's share of a finished tile: TMEM lane quarter q (rows row0 + 32 q +
 // lane) and column half h of the 256-column accumulator at tmem_acc, with the next chunk's
-// TMEM read and C-operand loads in flight under the current chunk's math.
+// TMEM read and C-operand loads in flight under the current chunk's math and stores.
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int64_t b, int64_t row0, int64_t n0,
-                                              int q, int h, int lane) {
+                                              int q, int h, int lane, uint8_t* stage) {
   constexpr int CHUNKS = BN / 2 / EPI_CW;
   float alpha = p.alpha, beta = p.beta;
   if (p.scale != nullptr) {
@@ -223,39 +269,41 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc
     if (p.alpha_pow == 1) alpha *= s; else if (p.alpha_pow == 2) alpha *= s * s;
     if (p.beta_pow == 1) beta *= s;
   }
-  const int64_t row = row0 + q * 32 + lane;
   const bool use_c = p.c != nullptr && beta != 0.f;
-  EpiRow er;
+  EpiRows er;
   er.d = p.d + b * p.d_bstride;
-  er.drow = er.d + row * p.ldd;
-  er.crow = use_c ? p.c + b * p.c_bstride + row * p.ldc : nullptr;
-  er.row = row;
-  er.ok = row < p.M;
+  er.c = use_c ? p.c + b * p.c_bstride : nullptr;
+  er.rbase = row0 + q * 32;
+  er.row = er.rbase + lane;
   const int64_t cbase = n0 + h * (BN / 2);
   const uint32_t tbase = tmem_acc + static_cast<uint32_t>(h * (BN / 2)) + (static_cast<uint32_t>(q * 32) << 16);
   uint32_t v[EPI_CW], vn[EPI_CW];
-  U16x8 cv[EPI_G], cvn[EPI_G];
+  uint4 creg[4];
   __syncwarp();
-  tc::tmem_ld_32x32b_x16(tbase, v);
-  load_c_chunk(p, er, cbase, cv);
+  tc::tmem_ld_32x32b_x32(tbase, v);
+  if (use_c) load_c_coalesced(p, er, cbase, lane, creg);
   tc::tmem_ld_wait();
-#pragma unroll
+#pragma unroll 1
   for (int cc = 0; cc < CHUNKS; ++cc) {
-    if (cc + 1 < CHUNKS) {
+    const int64_t col0 = cbase + cc * EPI_CW;
+    if (use_c) {
+      c_to_stage(stage, creg, lane);
       __syncwarp();
-      tc::tmem_ld_32x32b_x16(tbase + (cc + 1) * EPI_CW, vn);
-      load_c_chunk(p, er, cbase + (cc + 1) * EPI_CW, cvn);
     }
-    store_chunk(p, er, cbase + cc * EPI_CW, v, cv, alpha, beta);
+    if (cc + 1 < CHUNKS) {
+      tc::tmem_ld_32x32b_x32(tbase + (cc + 1) * EPI_CW, vn);
+      if (use_c) load_c_coalesced(p, er, col0 + EPI_CW, lane, creg);
+    }
+    chunk_math(p, use_c, v, alpha, beta, stage, lane);
+    __syncwarp();
+    if (col0 < p.N) store_chunk(p, er, stage, col0, lane);
+    __syncwarp();
     if (cc + 1 < CHUNKS) {
       tc::tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < EPI_CW; ++j) v[j] = vn[j];
-#pragma unroll
-      for (int j = 0; j < EPI_G; ++j) cv[j] = cvn[j];
     }
   }
-  __syncwarp();
 }
 
 template <int A_MN, int B_MN>
@@ -414,7 +462,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc::fence_after_sync();
       int64_t b, m0, n0;
       decode_tile<BM>(p, t, b, m0, n0);
-      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0, n0, q, h, lane, S.epi[warp - 4]);
       tc::fence_before_sync();
       tc::mbar_arrive(&S.tmem_empty[acc]);
       if (++acc == 2) {
@@ -459,6 +507,7 @@ constexpr uint16_t BOTH = 0x3;
 
 struct SharedStorage {
   alignas(1024) uint8_t stage[STAGES][STAGE_BYTES];
+  alignas(16) uint8_t epi[EPI_WARPS][EPI_STAGE_BYTES];  // epilogue staging, one buffer per warp
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full[2];
@@ -656,7 +705,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc::fence_after_sync();
       int64_t b, m0, n0;
       decode_tile<TILE_M>(p, t, b, m0, n0);
-      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane);
+      epilogue_tile(p, tmem_base + static_cast<uint32_t>(acc * BN), b, m0 + HALF * rank, n0, q, h, lane,
+                    S.epi[warp - 4]);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_cluster(leader_empty[acc]);
