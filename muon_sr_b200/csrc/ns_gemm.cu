@@ -157,8 +157,23 @@ __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device
 // lanes reading 8 rows at one group; 8 lanes writing 2 rows x 4 groups) free of bank
 // conflicts.
 
-__device__ __forceinline__ uint4* epi_slot(uint8_t* stage, int r, int g) {
-  return reinterpret_cast<uint4*>(stage + r * EPI_ROW_BYTES + ((g ^ ((r >> 1) & 3)) << 4));
+// Shared-memory address of group g of row r in a warp's buffer (stage: its shared address).
+// The accesses are explicit 16-byte shared loads and stores (the buffer is reached through a
+// generic pointer, which would otherwise leave the access width to the compiler).
+__device__ __forceinline__ uint32_t epi_slot(uint32_t stage, int r, int g) {
+  return stage + static_cast<uint32_t>(r * EPI_ROW_BYTES + ((g ^ ((r >> 1) & 3)) << 4));
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // The warp's view of one output tile: rows [rbase, rbase + 32) of matrix b, and this lane's
@@ -190,21 +205,21 @@ __device__ __forceinline__ void load_c_coalesced(const Params& p, const EpiRows&
 }
 
 // Coalesced C registers -> staging buffer (row r of the warp at row r of the buffer).
-__device__ __forceinline__ void c_to_stage(uint8_t* stage, const uint4 (&creg)[4], int lane) {
+__device__ __forceinline__ void c_to_stage(uint32_t stage, const uint4 (&creg)[4], int lane) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) *epi_slot(stage, i * 8 + (lane >> 2), lane & 3) = creg[i];
+  for (int i = 0; i < 4; ++i) sts128(epi_slot(stage, i * 8 + (lane >> 2), lane & 3), creg[i]);
 }
 
 // Epilogue math for this lane's row, columns [col0, col0 + EPI_CW), in place in the staging
 // buffer: each 16-byte group of the row is read (the C operand, when used) and overwritten
 // with the output by this lane alone.
 __device__ __forceinline__ void chunk_math(const Params& p, bool use_c, const uint32_t (&v)[EPI_CW], float alpha,
-                                           float beta, uint8_t* stage, int lane) {
+                                           float beta, uint32_t stage, int lane) {
 #pragma unroll
   for (int g = 0; g < EPI_G; ++g) {
-    uint4* slot = epi_slot(stage, lane, g);
+    const uint32_t slot = epi_slot(stage, lane, g);
     U16x8 cv, o;
-    if (use_c) *reinterpret_cast<uint4*>(cv.v) = *slot;
+    if (use_c) *reinterpret_cast<uint4*>(cv.v) = lds128(slot);
     if (p.ref_round) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -217,21 +232,21 @@ __device__ __forceinline__ void chunk_math(const Params& p, bool use_c, const ui
       for (int j = 0; j < 8; ++j)
         o.v[j] = rne_bf16_bits(fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * (use_c ? bf16_bits_to_f32(cv.v[j]) : 0.f)));
     }
-    *slot = *reinterpret_cast<const uint4*>(o.v);
+    sts128(slot, *reinterpret_cast<const uint4*>(o.v));
   }
 }
 
 // The chunk's output rows in the staging buffer -> coalesced stores of the warp's 32 rows;
 // then, in symmetric mode, the mirror of the strictly-upper elements: (row, c) -> (c, row).
 // Lanes hold consecutive rows, so each mirrored column's stores form one 64-byte segment.
-__device__ __forceinline__ void store_chunk(const Params& p, const EpiRows& er, uint8_t* stage, int64_t col0,
+__device__ __forceinline__ void store_chunk(const Params& p, const EpiRows& er, uint32_t stage, int64_t col0,
                                             int lane) {
   const int64_t col = col0 + (lane & 3) * 8;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = i * 8 + (lane >> 2);
     const int64_t row = er.rbase + r;
-    const uint4 w = *epi_slot(stage, r, lane & 3);
+    const uint4 w = lds128(epi_slot(stage, r, lane & 3));
     if (row < p.M && col + 8 <= p.N) {
       *reinterpret_cast<uint4*>(er.d + row * p.ldd + col) = w;
     } else if (row < p.M) {
@@ -246,7 +261,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRows& er, 
 #pragma unroll
     for (int g = 0; g < EPI_G; ++g) {
       U16x8 o;
-      *reinterpret_cast<uint4*>(o.v) = *epi_slot(stage, lane, g);
+      *reinterpret_cast<uint4*>(o.v) = lds128(epi_slot(stage, lane, g));
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int64_t c = col0 + g * 8 + j;
@@ -260,7 +275,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, const EpiRows& er, 
 // lane) and column half h of the 256-column accumulator at tmem_acc, with the next chunk's
 // TMEM read and C-operand loads in flight under the current chunk's math and stores.
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int64_t b, int64_t row0, int64_t n0,
-                                              int q, int h, int lane, uint8_t* stage) {
+                                              int q, int h, int lane, uint8_t* stage_ptr) {
+  const uint32_t stage = tc::smem_addr(stage_ptr);
   constexpr int CHUNKS = BN / 2 / EPI_CW;
   float alpha = p.alpha, beta = p.beta;
   if (p.scale != nullptr) {
