@@ -177,7 +177,7 @@ class _Work:
         return self.owner is None or self.owner(stack_idx, row)
 
 
-def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work=None):
+def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, seeder, work=None, after_first=None):
     """Batched step over the shape stacks (``_triton_muon_batch_step``,
     triton_muon_sr.py:128-177).
 
@@ -193,7 +193,8 @@ def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, se
     are shared as they are finished. Without ``work``, stacks of small matrices (smaller
     dimension <= CONCURRENT_MAX_DIM) run on side streams that start with the step and join the
     current stream at its end; every stack touches only its own tensors, so the bits do not
-    depend on the overlap."""
+    depend on the overlap. ``after_first`` (if given) is called once, after the first stack
+    issued on the current stream (or at the end when there is none)."""
     work = work or _Work()
     order = list(enumerate(stacks.by_shape.items()))
     if work.share is not None and not seeder.random:
@@ -221,8 +222,13 @@ def muon_batch_step(stacks, beta, nesterov, ns_steps, lr, weight_decay, step, se
         else:
             _stack_step(s, shape, members, stacks.tensor[shape], beta, nesterov, ns_steps, lr, weight_decay, step,
                         seeder, work)
+            if after_first is not None:
+                after_first()
+                after_first = None
         if work.share is not None:
             work.share(members)
+    if after_first is not None:
+        after_first()
     for side in dict.fromkeys(used):
         main.wait_stream(side)
 
@@ -376,7 +382,7 @@ class _MuonBase(Optimizer):
         super().load_state_dict(state_dict)
         self._reset_batched()
 
-    def _run_muon_group(self, gi, group, batched, batched_groups, seeder):
+    def _run_muon_group(self, gi, group, batched, batched_groups, seeder, after_first=None):
         name = type(self).__name__
         beta, nesterov, ns_steps = group["momentum"], group["nesterov"], group["ns_steps"]
         lr, wd = group["lr"], group["weight_decay"]
@@ -389,7 +395,7 @@ class _MuonBase(Optimizer):
                 _validate(p, name)
             step = self._clock.advance(self.state, batched_groups, group["params"]) if self._record_step else 0
             work = _Work(sh.muon_owner(gi, stacks.by_shape), sh.share, sh.segments, sh.update_stream) if sh else None
-            muon_batch_step(stacks, beta, nesterov, ns_steps, lr, wd, step, seeder, work)
+            muon_batch_step(stacks, beta, nesterov, ns_steps, lr, wd, step, seeder, work, after_first)
             return
         for i, p in enumerate(group["params"]):
             _validate(p, name)
@@ -408,6 +414,11 @@ class _MuonBase(Optimizer):
                 seeder.skip(step, i, 1)
                 continue
             muon_single_step(p, st["momentum_buffer"], beta, nesterov, ns_steps, lr, wd, step, i, seeder)
+            if after_first is not None:
+                after_first()
+                after_first = None
+        if after_first is not None:
+            after_first()
         if sh:
             sh.share(group["params"])
 
@@ -500,12 +511,9 @@ class TritonMuonSRWithAuxAdam(_MuonBase):
             # every group's math is independent of the processing order (seeds drawn from
             # torch's generator are not: those classes keep the order).
             order = sorted(order, key=lambda gi: bool(groups[gi]["use_muon"]))
-        for gi in order:
+
+        def adam(gi):
             group = groups[gi]
-            if group["use_muon"]:
-                if group["params"]:
-                    self._run_muon_group(gi, group, self.batch_ns, muon_groups, seeder)
-                continue
             side = sh.update_stream if sh else None
             with torch.cuda.stream(side) if side is not None else _nullctx():
                 # (multicast weights: the AdamW updates run under the Muon groups' GEMMs)
@@ -513,6 +521,30 @@ class TritonMuonSRWithAuxAdam(_MuonBase):
                                  owns=(lambda i, gi=gi: sh.owns(gi, i)) if sh else None)
             if sh:
                 sh.share(group["params"])
+
+        # Fed from host memory (HostStaging), the AdamW groups run right after the first Muon
+        # stack: the download of their weights then overlaps the remaining Newton-Schulz work
+        # instead of trailing the step, and their uploads queue behind that stack's. Bits do
+        # not depend on the order; seeds drawn from torch's generator do, so those classes
+        # keep it.
+        deferred = [gi for gi in order if not groups[gi]["use_muon"]] \
+            if staging.active() and not sh and not self._random_seeds and muon_groups else []
+        skip = set(deferred)
+
+        def run_deferred():
+            while deferred:
+                adam(deferred.pop(0))
+
+        for gi in order:
+            group = groups[gi]
+            if group["use_muon"]:
+                if group["params"]:
+                    self._run_muon_group(gi, group, self.batch_ns, muon_groups, seeder,
+                                         after_first=run_deferred if deferred else None)
+                continue
+            if gi not in skip:
+                adam(gi)
+        run_deferred()
         if sh:
             sh.sync_params(self)
         return loss

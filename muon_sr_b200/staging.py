@@ -34,6 +34,11 @@ _tls = threading.local()
 BATCH_NUMEL = 1 << 28
 
 
+def active():
+    """Whether a HostStaging step is being issued on this thread."""
+    return getattr(_tls, "io", None) is not None
+
+
 def need(params):
     """Announce that the next launch reads the gradients of ``params``."""
     io = getattr(_tls, "io", None)

@@ -366,6 +366,53 @@ def test_batched_step_staging_hooks(monkeypatch):
     assert ctrs == [r * 128 for r in range(5)] + [r * 128 for r in range(3)]
 
 
+@pytest.mark.parametrize("adam_first", [False, True])
+def test_hybrid_staging_order(monkeypatch, adam_first):
+    """Under HostStaging a deterministic-seed hybrid step runs its AdamW group once, right
+    after the first Muon stack (so the AdamW weights download under the later stacks);
+    without staging, and for the classes seeded from torch's generator, the group order
+    stands."""
+    import muon_sr_b200.muon as M
+    import muon_sr_b200.staging as S
+    from muon_sr_b200 import MuonSRWithAuxAdam, TritonMuonSRWithAuxAdam
+    shapes = [(8, 16)] * 3 + [(16, 8)] * 2 + [(4,), (6,)]
+    params = [torch.nn.Parameter(torch.zeros(*s, dtype=torch.bfloat16)) for s in shapes]
+    for p in params:
+        p.grad = torch.zeros_like(p)
+    names = {id(p): i for i, p in enumerate(params)}
+    log = []
+    monkeypatch.setattr(M, "NS_CHUNK_NUMEL", 256)   # 2 matrices per chunk
+    monkeypatch.setattr(M.K, "muon_prepare", lambda items, b, n: None)
+    monkeypatch.setattr(M.K, "newton_schulz", lambda x, steps: torch.zeros_like(x))
+    monkeypatch.setattr(M.K, "muon_apply", lambda items, lr, wd: None)
+    import muon_sr_b200.adamw as A
+    monkeypatch.setattr(A.K, "adamw_sr", lambda batch, *a: log.append(("adamw", [names[id(e[0])] for e in batch])))
+    muon = dict(params=params[:5], use_muon=True, lr=0.02)
+    adam = dict(params=params[5:], use_muon=False, lr=3e-4)
+
+    def run(cls, staged):
+        log.clear()
+        opt = cls([adam, muon] if adam_first else [muon, adam], batch_ns=True)
+        if staged:
+            monkeypatch.setattr(S._tls, "io", _RecordingIO(log, names), raising=False)
+        try:
+            opt.step()
+        finally:
+            monkeypatch.setattr(S._tls, "io", None, raising=False)
+        return [(k, v) for k, v in log if k != "need"]
+
+    staged = run(TritonMuonSRWithAuxAdam, True)
+    # first stack (3 matrices: chunks 2 + 1), then the AdamW group, then the second stack
+    assert staged == [("done", [0, 1]), ("done", [2]), ("adamw", [5, 6]), ("done", [5, 6]),
+                      ("done", [3, 4])]
+    plain = run(TritonMuonSRWithAuxAdam, False)
+    assert plain == [("adamw", [5, 6])]
+    seeded = run(MuonSRWithAuxAdam, True)
+    adam_at = seeded.index(("adamw", [5, 6]))
+    assert adam_at == (0 if adam_first else len(seeded) - 2)
+    assert [v for k, v in seeded if k == "adamw"] == [[5, 6]]
+
+
 def test_staging_batches():
     """Launch batches are cut only while a staging step runs, at whole items."""
     import muon_sr_b200.staging as S
