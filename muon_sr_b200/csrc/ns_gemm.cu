@@ -153,9 +153,9 @@ __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_msr_device
 // operand and the output pass through a 2 KB staging buffer per warp in shared memory, so
 // that each global access instruction covers 8 rows x 64 contiguous bytes (lane l moves the
 // 16-byte group l % 4 of row l / 4 + 8 i in pass i). The buffer holds 32 rows of 64 bytes;
-// group g of row r sits at slot g ^ ((r >> 1) & 3), which keeps both access patterns (8
-// lanes reading 8 rows at one group; 8 lanes writing 2 rows x 4 groups) free of bank
-// conflicts.
+// group g of row r sits at slot g ^ ((r >> 1) & 3), which gives 8 consecutive lanes 8
+// distinct 16-byte bank groups in both access patterns (8 lanes at one group of 8 rows; 8
+// lanes at 4 groups of 2 rows).
 
 // Shared-memory address of group g of row r in a warp's buffer (stage: its shared address).
 // The accesses are explicit 16-byte shared loads and stores (the buffer is reached through a
@@ -230,7 +230,8 @@ __device__ __forceinline__ void chunk_math(const Params& p, bool use_c, const ui
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        o.v[j] = rne_bf16_bits(fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * (use_c ? bf16_bits_to_f32(cv.v[j]) : 0.f)));
+        o.v[j] = rne_bf16_bits(
+            fmaf(alpha, __uint_as_float(v[g * 8 + j]), beta * (use_c ? bf16_bits_to_f32(cv.v[j]) : 0.f)));
     }
     sts128(slot, *reinterpret_cast<const uint4*>(o.v));
   }
